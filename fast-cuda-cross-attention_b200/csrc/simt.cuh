@@ -1,0 +1,184 @@
+// Generic CUDA-core kernels: the shape-agnostic attention path (any D, any key range,
+// fp32 / fp16 / bf16 inputs, strided per-head views), the log-sum-exp combine of split
+// partials (upstream kernel_splitk.cu:186-236) and the helpers of the multi-GPU merge.
+//
+// The generic attention kernel is the GPU path for shapes the tcgen05 kernels do not
+// take (D not a multiple of 64, D > 768, ...).  It is correct for every shape and never
+// used where a tensor-core kernel applies.  One warp owns one query row; keys are
+// consumed one at a time with an online softmax in the log2 domain; the query row and
+// the output accumulator live in shared memory so D is bounded only by shared memory.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sm100.cuh"
+
+namespace xattn {
+namespace simt {
+
+__device__ __forceinline__ float to_f(float x) { return x; }
+__device__ __forceinline__ float to_f(__half x) { return __half2float(x); }
+__device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ void from_f(float* d, float x) { *d = x; }
+__device__ __forceinline__ void from_f(__nv_bfloat16* d, float x) { *d = __float2bfloat16_rn(x); }
+
+template <typename Tin, typename Tout>
+struct Args {
+  const Tin* q;
+  const Tin* k;
+  const Tin* v;
+  Tout* out;          // final mode
+  float* po;          // split mode: [B*H][Nl][S][dh] (flattened like the upstream layout)
+  float* pm;
+  float* pl;
+  long long q_bs, k_bs, o_bs;  // batch strides (elements)
+  int ld_q, ld_k, ld_o;        // row strides (elements)
+  int heads, dh;               // head h reads columns [h*dh, (h+1)*dh)
+  int n_latent, n_input;
+  int num_splits, split_chunk, split_mode;
+  float scale_log2;            // log2(e) * softmax scale
+};
+
+constexpr int kWarps = 4;
+
+template <typename Tin, typename Tout>
+__global__ void __launch_bounds__(kWarps * 32) attention_kernel(const Args<Tin, Tout> a) {
+  extern __shared__ float sm[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int row = blockIdx.x * kWarps + warp;
+  const int bh = blockIdx.y;
+  const int split = blockIdx.z;
+  const int b = bh / a.heads, hd = bh % a.heads;
+  float* qs = sm + warp * 2 * a.dh;
+  float* os = qs + a.dh;
+  const bool live = row < a.n_latent;
+  const int k0 = split * a.split_chunk;
+  const int k1 = min(k0 + a.split_chunk, a.n_input);
+  if (live) {
+    const Tin* qr = a.q + b * a.q_bs + static_cast<long long>(row) * a.ld_q + hd * a.dh;
+    for (int d = lane; d < a.dh; d += 32) {
+      qs[d] = to_f(qr[d]);
+      os[d] = 0.f;
+    }
+  }
+  __syncwarp();
+  float m = -INFINITY, l = 0.f;
+  if (live) {
+    for (int key = k0; key < k1; ++key) {
+      const Tin* kr = a.k + b * a.k_bs + static_cast<long long>(key) * a.ld_k + hd * a.dh;
+      float dot = 0.f;
+      for (int d = lane; d < a.dh; d += 32) dot = fmaf(qs[d], to_f(kr[d]), dot);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      const float t = dot * a.scale_log2;
+      const float mn = fmaxf(m, t);
+      const float alpha = exp2f(m - mn);
+      const float pw = exp2f(t - mn);
+      l = l * alpha + pw;
+      m = mn;
+      const Tin* vr = a.v + b * a.k_bs + static_cast<long long>(key) * a.ld_k + hd * a.dh;
+      for (int d = lane; d < a.dh; d += 32) os[d] = fmaf(os[d], alpha, pw * to_f(vr[d]));
+    }
+  }
+  __syncwarp();
+  if (!live) return;
+  if (a.split_mode) {
+    const size_t pidx = (static_cast<size_t>(bh) * a.n_latent + row) * a.num_splits + split;
+    float* dst = a.po + pidx * a.dh;
+    if (k1 > k0) {
+      for (int d = lane; d < a.dh; d += 32) dst[d] = os[d];
+      if (lane == 0) {
+        a.pm[pidx] = m * 0.69314718055994531f;
+        a.pl[pidx] = l;
+      }
+    } else {
+      for (int d = lane; d < a.dh; d += 32) dst[d] = 0.f;
+      if (lane == 0) {
+        a.pm[pidx] = -3.4028234663852886e38f;
+        a.pl[pidx] = 0.f;
+      }
+    }
+  } else {
+    const float inv = 1.f / l;
+    Tout* dst = a.out + b * a.o_bs + static_cast<long long>(row) * a.ld_o + hd * a.dh;
+    for (int d = lane; d < a.dh; d += 32) from_f(&dst[d], os[d] * inv);
+  }
+}
+
+// Log-sum-exp merge of S split partials per row (upstream kernel_splitk.cu:186-236):
+// M = max_s m_s; L = sum_s e^(m_s-M) l_s; O = sum_s e^(m_s-M) O_s / L.  Splits whose
+// m is -FLT_MAX (empty) are skipped.  One warp per row, any D.
+template <typename Tout>
+__global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ po,
+                                                      const float* __restrict__ pm,
+                                                      const float* __restrict__ pl,
+                                                      Tout* __restrict__ out, long long rows,
+                                                      int dim, int num_splits, int ld_o) {
+  const long long r = static_cast<long long>(blockIdx.x) * 4 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= rows) return;
+  const float* m = pm + r * num_splits;
+  const float* l = pl + r * num_splits;
+  float mx = -INFINITY;
+  for (int s = 0; s < num_splits; ++s)
+    if (m[s] > -3.4028234663852886e38f) mx = fmaxf(mx, m[s]);
+  float lsum = 0.f;
+  for (int s = 0; s < num_splits; ++s)
+    if (m[s] > -3.4028234663852886e38f) lsum += __expf(m[s] - mx) * l[s];
+  const float inv = 1.f / lsum;
+  Tout* dst = out + r * static_cast<long long>(ld_o);
+  for (int d = lane; d < dim; d += 32) {
+    float acc = 0.f;
+    for (int s = 0; s < num_splits; ++s) {
+      if (!(m[s] > -3.4028234663852886e38f)) continue;
+      acc = fmaf(__expf(m[s] - mx), po[(r * num_splits + s) * dim + d], acc);
+    }
+    from_f(&dst[d], acc * inv);
+  }
+}
+
+// Multi-GPU N_input split, step 2: after an all-reduce MAX of the row maxima into
+// `mglob`, rescale this rank's partial to the global max in place:
+//   O <- O * e^(m - M),  l <- l * e^(m - M).
+// Rows are packed as [rows][dim + 1] with l in the last column, so one SUM all-reduce
+// merges O and l together.
+__global__ void __launch_bounds__(128) lse_rescale_kernel(float* __restrict__ ol,
+                                                          const float* __restrict__ m_local,
+                                                          const float* __restrict__ m_glob,
+                                                          long long rows, int dim) {
+  const long long r = static_cast<long long>(blockIdx.x) * 4 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= rows) return;
+  const float ml = m_local[r];
+  const float f = ml > -3.4028234663852886e38f ? __expf(ml - m_glob[r]) : 0.f;
+  float* row = ol + r * (dim + 1);
+  for (int d = lane; d <= dim; d += 32) row[d] *= f;
+}
+
+// Multi-GPU N_input split, step 4: out = O / l from the summed [rows][dim + 1] buffer.
+__global__ void __launch_bounds__(128) lse_finalize_kernel(const float* __restrict__ ol,
+                                                           float* __restrict__ out,
+                                                           long long rows, int dim) {
+  const long long r = static_cast<long long>(blockIdx.x) * 4 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= rows) return;
+  const float* row = ol + r * (dim + 1);
+  const float inv = 1.f / row[dim];
+  for (int d = lane; d < dim; d += 32) out[r * dim + d] = row[d] * inv;
+}
+
+// Pack split-mode partials (po [rows][dim], pl [rows]) into [rows][dim + 1].
+__global__ void __launch_bounds__(128) lse_pack_kernel(const float* __restrict__ po,
+                                                       const float* __restrict__ pl,
+                                                       float* __restrict__ ol, long long rows,
+                                                       int dim) {
+  const long long r = static_cast<long long>(blockIdx.x) * 4 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (r >= rows) return;
+  for (int d = lane; d < dim; d += 32) ol[r * (dim + 1) + d] = po[r * dim + d];
+  if (lane == 0) ol[r * (dim + 1) + dim] = pl[r];
+}
+
+}  // namespace simt
+}  // namespace xattn

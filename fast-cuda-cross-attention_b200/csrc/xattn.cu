@@ -1,0 +1,519 @@
+// kernels.so: the C ABI declared in include/xattn.h and the host-side dispatch behind it.
+//
+// Path selection for an fp32 call (Q, K, V, O fp32, row-major, contiguous):
+//   * tensor-core path (fused_tf32.cuh) when D is a multiple of 64 in [64, 768] and the
+//     four pointers are 16-byte aligned (TMA requirement); a key split with a library
+//     workspace is added automatically when batch * ceil(N_latent/128) row blocks cannot
+//     fill the GPU's SMs;
+//   * generic CUDA-core path (simt.cuh) otherwise.
+// There is no host fallback: every path is a GPU kernel.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "fused_tf32.cuh"
+#include "simt.cuh"
+#include "sm100.cuh"
+#include "tmap.h"
+#include "xattn.h"
+
+namespace xattn {
+namespace {
+
+constexpr int kVersion = 10000;  // 1.0.0
+constexpr float kLog2e = 1.4426950408889634f;
+// Mean relative truncation error of one TF32 operand for log-uniform mantissas:
+// 2^-11 * E[1/m], E[1/m] = 1 / (2 ln 2) for m log-uniform on [1, 2).
+constexpr double kTf32TruncBias = 0.00048828125 * 0.72134752044448170;
+
+thread_local int t_last_error = XATTN_OK;
+std::atomic<int> g_opt_path{0};
+std::atomic<int> g_opt_splits{0};
+std::atomic<int> g_opt_wait_us{2000000};
+std::atomic<int> g_opt_tf32_comp{1};
+
+int set_error(int code) {
+  t_last_error = code;
+  return code;
+}
+
+// ------------------------------------------------------------------ per-device state
+struct DeviceState {
+  bool init = false;
+  int sms = 148;
+  int wait_us = -1;  // value last copied into g_wait_ns on this device
+};
+std::mutex g_mu;
+DeviceState g_dev[64];
+
+// One-time per-device setup: kernel attributes and the device wait bound.
+int prepare_device(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return XATTN_ERR_LAUNCH;
+  *dev_out = dev;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& st = g_dev[dev];
+  if (!st.init) {
+    cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaFuncSetAttribute(fused::fused_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             fused::kSmemBytes) != cudaSuccess)
+      return XATTN_ERR_LAUNCH;
+    st.init = true;
+  }
+  const int want = g_opt_wait_us.load();
+  if (st.wait_us != want) {
+    const unsigned long long ns = static_cast<unsigned long long>(want) * 1000ull;
+    if (cudaMemcpyToSymbol(g_wait_ns, &ns, sizeof(ns)) != cudaSuccess) return XATTN_ERR_LAUNCH;
+    st.wait_us = want;
+  }
+  return XATTN_OK;
+}
+
+int sm_count(int dev) { return g_dev[dev].sms > 0 ? g_dev[dev].sms : 148; }
+
+// Library workspace for automatic key splits: one grow-only buffer per (device, stream).
+// Calls that share a stream are ordered by it; different streams get different buffers.
+struct Workspace {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+
+void* workspace(int dev, cudaStream_t stream, size_t bytes) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace& w = g_ws[{dev, stream}];
+  if (w.bytes >= bytes) return w.ptr;
+  if (w.ptr != nullptr) {
+    cudaStreamSynchronize(stream);
+    cudaFree(w.ptr);
+    w.ptr = nullptr;
+    w.bytes = 0;
+  }
+  size_t grow = std::max(bytes, static_cast<size_t>(16) << 20);
+  if (cudaMalloc(&w.ptr, grow) != cudaSuccess) {
+    w.ptr = nullptr;
+    return nullptr;
+  }
+  w.bytes = grow;
+  return w.ptr;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ------------------------------------------------------------------ tensor-core fp32 path
+bool tc_fp32_supported(const float* Q, const float* K, const float* V, const float* O, int D) {
+  return D >= 64 && D <= 2 * fused::kMaxDh && D % 64 == 0 && aligned16(Q) && aligned16(K) &&
+         aligned16(V) && (O == nullptr || aligned16(O));
+}
+
+bool make_fp32_maps(fused::Params& p, const float* Q, const float* K, const float* V, int B,
+                    int Nl, int Ni, int D) {
+  const uint64_t dq[3] = {(uint64_t)D, (uint64_t)Nl, (uint64_t)B};
+  const uint64_t sq[2] = {(uint64_t)D * 4, (uint64_t)Nl * D * 4};
+  const uint64_t dk[3] = {(uint64_t)D, (uint64_t)Ni, (uint64_t)B};
+  const uint64_t sk[2] = {(uint64_t)D * 4, (uint64_t)Ni * D * 4};
+  const uint32_t bq[3] = {fused::kChunk, fused::kRows, 1};
+  const uint32_t bk[3] = {fused::kChunk, fused::kKeys, 1};
+  const uint32_t bv[3] = {fused::kChunk, fused::kVKeys, 1};
+  return encode_tmap(&p.tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, Q, dq, sq, bq,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+         encode_tmap(&p.tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, K, dk, sk, bk,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+         encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, V, dk, sk, bv,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+}
+
+// Launch the fused kernel.  split_mode = 0: normalised output `out`; 1: partials.
+int launch_fused(const float* Q, const float* K, const float* V, float* out, float* po,
+                 float* pm, float* pl, int B, int Nl, int Ni, int D, int num_splits,
+                 int split_chunk, int split_mode, cudaStream_t stream) {
+  fused::Params p;
+  if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D)) return XATTN_ERR_ARG;
+  p.out = out;
+  p.po = po;
+  p.pm = pm;
+  p.pl = pl;
+  p.batch = B;
+  p.n_latent = Nl;
+  p.n_input = Ni;
+  p.dim = D;
+  p.dh = D / 2;
+  p.n_row_blocks = (Nl + fused::kRows - 1) / fused::kRows;
+  p.num_splits = num_splits;
+  p.split_chunk = split_chunk;
+  p.split_mode = split_mode;
+  const bool comp = g_opt_tf32_comp.load() != 0;
+  p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(D)) *
+                                    (comp ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
+  p.out_comp = comp ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+  const long long items = static_cast<long long>(B) * p.n_row_blocks * num_splits;
+  if (items * 2 > 0x7fffffffLL) return XATTN_ERR_ARG;
+  fused::fused_tf32_kernel<<<static_cast<unsigned>(items * 2), fused::kThreads, fused::kSmemBytes,
+                             stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+// ------------------------------------------------------------------ generic path
+template <typename Tin, typename Tout>
+int launch_simt(const Tin* Q, const Tin* K, const Tin* V, Tout* out, float* po, float* pm,
+                float* pl, int B, int heads, int Nl, int Ni, int dh, int num_splits,
+                int split_chunk, int split_mode, float scale_log2, cudaStream_t stream) {
+  simt::Args<Tin, Tout> a;
+  a.q = Q;
+  a.k = K;
+  a.v = V;
+  a.out = out;
+  a.po = po;
+  a.pm = pm;
+  a.pl = pl;
+  const int ld = heads * dh;
+  a.q_bs = static_cast<long long>(Nl) * ld;
+  a.k_bs = static_cast<long long>(Ni) * ld;
+  a.o_bs = static_cast<long long>(Nl) * ld;
+  a.ld_q = a.ld_k = a.ld_o = ld;
+  a.heads = heads;
+  a.dh = dh;
+  a.n_latent = Nl;
+  a.n_input = Ni;
+  a.num_splits = num_splits;
+  a.split_chunk = split_chunk;
+  a.split_mode = split_mode;
+  a.scale_log2 = scale_log2;
+  const size_t smem = static_cast<size_t>(simt::kWarps) * 2 * dh * sizeof(float);
+  auto kern = simt::attention_kernel<Tin, Tout>;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+          cudaSuccess)
+    return XATTN_ERR_ARG;
+  dim3 grid((Nl + simt::kWarps - 1) / simt::kWarps, B * heads, num_splits);
+  kern<<<grid, simt::kWarps * 32, smem, stream>>>(a);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+int launch_combine(const float* po, const float* pm, const float* pl, float* out, long long rows,
+                   int D, int num_splits, cudaStream_t stream) {
+  if (rows <= 0) return XATTN_OK;
+  const long long blocks = (rows + 3) / 4;
+  simt::combine_kernel<float><<<static_cast<unsigned>(blocks), 128, 0, stream>>>(
+      po, pm, pl, out, rows, D, num_splits, D);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+bool bad_sizes(int B, int Nl, int Ni, int D) { return B < 0 || Nl < 0 || Ni < 0 || D <= 0; }
+
+// Upstream semantics for N_input == 0: softmax over no keys gives an empty weight row and
+// bmm with an empty V gives zeros (generate_references.py:17-23 evaluated at Ni = 0).
+int zero_output(float* O, int B, int Nl, int D, cudaStream_t stream) {
+  const size_t bytes = static_cast<size_t>(B) * Nl * D * sizeof(float);
+  if (bytes == 0) return XATTN_OK;
+  return cudaMemsetAsync(O, 0, bytes, stream) == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+// Key-split plan of the automatic fp32 path: one pass when batch * row blocks fill the
+// two-CTA cluster slots (SMs / 2), otherwise enough tile-aligned splits to fill them.
+void plan_splits(int dev, int B, int Nl, int Ni, int path, int* splits_out, int* chunk_out) {
+  const int n_rb = (Nl + fused::kRows - 1) / fused::kRows;
+  const long long items = static_cast<long long>(B) * n_rb;
+  const int n_tiles = (Ni + fused::kKeys - 1) / fused::kKeys;
+  const int slots = std::max(1, sm_count(dev) / 2);
+  int splits = g_opt_splits.load();
+  if (splits <= 0) {
+    splits = 1;
+    if (path == 0 && items < slots)
+      splits = static_cast<int>(std::min<long long>(n_tiles, slots / std::max(1LL, items)));
+  }
+  splits = std::max(1, std::min(splits, std::max(1, n_tiles)));
+  const int tiles_per = (n_tiles + splits - 1) / splits;
+  int chunk = std::max(1, tiles_per) * fused::kKeys;
+  splits = std::max(1, (Ni + chunk - 1) / chunk);
+  if (splits == 1) chunk = Ni;
+  *splits_out = splits;
+  *chunk_out = chunk;
+}
+
+// The fp32 entry: all four upstream fp32 names and xattn_fp32 land here.
+int run_fp32(const float* Q, const float* K, const float* V, float* O, int B, int Nl, int Ni,
+             int D, cudaStream_t stream) {
+  if (bad_sizes(B, Nl, Ni, D)) return set_error(XATTN_ERR_ARG);
+  if (B == 0 || Nl == 0) return set_error(XATTN_OK);
+  if (O == nullptr) return set_error(XATTN_ERR_ARG);
+  if (Ni == 0) return set_error(zero_output(O, B, Nl, D, stream));
+  if (Q == nullptr || K == nullptr || V == nullptr) return set_error(XATTN_ERR_ARG);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return set_error(rc);
+  const int path = g_opt_path.load();
+  const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(D));
+  if (path == 2 || !tc_fp32_supported(Q, K, V, O, D)) {
+    return set_error(launch_simt<float, float>(Q, K, V, O, nullptr, nullptr, nullptr, B, 1, Nl, Ni,
+                                               D, 1, Ni, 0, scale_log2, stream));
+  }
+  int splits = 1, chunk = Ni;
+  plan_splits(dev, B, Nl, Ni, path, &splits, &chunk);
+  if (splits == 1)
+    return set_error(launch_fused(Q, K, V, O, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni, 0,
+                                  stream));
+  // Tile-aligned key split through the library workspace, then the log-sum-exp merge.
+  const size_t rows = static_cast<size_t>(B) * Nl;
+  const size_t po_elems = rows * splits * D;
+  const size_t ml_elems = rows * splits;
+  float* ws = static_cast<float*>(workspace(dev, stream, (po_elems + 2 * ml_elems + 64) * sizeof(float)));
+  if (ws == nullptr) return set_error(XATTN_ERR_NOMEM);
+  float* po = ws;
+  float* pm = po + po_elems;
+  float* pl = pm + ml_elems;
+  rc = launch_fused(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, splits, chunk, 1, stream);
+  if (rc != XATTN_OK) return set_error(rc);
+  return set_error(launch_combine(po, pm, pl, O, static_cast<long long>(rows), D, splits, stream));
+}
+
+int run_splitk(const float* Q, const float* K, const float* V, float* O, float* po, float* pm,
+               float* pl, int B, int Nl, int Ni, int D, int S, cudaStream_t stream) {
+  if (bad_sizes(B, Nl, Ni, D) || S <= 0) return set_error(XATTN_ERR_ARG);
+  if (B == 0 || Nl == 0) return set_error(XATTN_OK);
+  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr || po == nullptr ||
+      pm == nullptr || pl == nullptr)
+    return set_error(XATTN_ERR_ARG);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return set_error(rc);
+  const int chunk = std::max(1, (Ni + S - 1) / S);  // kernel_splitk.cu:59
+  const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(D));
+  if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, O, D) || !aligned16(po))
+    rc = launch_simt<float, float>(Q, K, V, nullptr, po, pm, pl, B, 1, Nl, Ni, D, S, chunk, 1,
+                                   scale_log2, stream);
+  else
+    rc = launch_fused(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, S, chunk, 1, stream);
+  if (rc != XATTN_OK) return set_error(rc);
+  return set_error(launch_combine(po, pm, pl, O, static_cast<long long>(B) * Nl, D, S, stream));
+}
+
+}  // namespace
+}  // namespace xattn
+
+using namespace xattn;
+
+// ===================================================================== Part 1: upstream ABI
+extern "C" void launch_naive_kernel(const float* Q, const float* K, const float* V, float* output,
+                                    int batch_size, int N_latent, int N_input, int dim,
+                                    cudaStream_t stream) {
+  run_fp32(Q, K, V, output, batch_size, N_latent, N_input, dim, stream);
+}
+
+extern "C" void launch_parallel_kernel(const float* Q, const float* K, const float* V,
+                                       float* output, int batch_size, int N_latent, int N_input,
+                                       int dim, cudaStream_t stream) {
+  run_fp32(Q, K, V, output, batch_size, N_latent, N_input, dim, stream);
+}
+
+extern "C" void launch_tiled_kernel(const float* Q, const float* K, const float* V, float* output,
+                                    int batch_size, int N_latent, int N_input, int dim,
+                                    cudaStream_t stream) {
+  run_fp32(Q, K, V, output, batch_size, N_latent, N_input, dim, stream);
+}
+
+extern "C" void launch_optimized_kernel(const float* Q, const float* K, const float* V,
+                                        float* output, int batch_size, int N_latent, int N_input,
+                                        int dim, cudaStream_t stream) {
+  run_fp32(Q, K, V, output, batch_size, N_latent, N_input, dim, stream);
+}
+
+extern "C" void launch_wmma_kernel(const __half* Q, const __half* K, const __half* V,
+                                   float* output, int batch_size, int N_latent, int N_input,
+                                   int dim, cudaStream_t stream) {
+  if (bad_sizes(batch_size, N_latent, N_input, dim)) { set_error(XATTN_ERR_ARG); return; }
+  if (batch_size == 0 || N_latent == 0) { set_error(XATTN_OK); return; }
+  if (N_input == 0) { set_error(zero_output(output, batch_size, N_latent, dim, stream)); return; }
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) { set_error(rc); return; }
+  // Q arrives pre-scaled by 1/sqrt(dim) (cuda_wrappers.py:635-640): score scale is 1.
+  set_error(launch_simt<__half, float>(Q, K, V, output, nullptr, nullptr, nullptr, batch_size, 1,
+                                       N_latent, N_input, dim, 1, N_input, 0, kLog2e, stream));
+}
+
+extern "C" void launch_splitk_kernel(const float* Q, const float* K, const float* V, float* output,
+                                     float* po, float* pm, float* pl, int batch_size, int N_latent,
+                                     int N_input, int dim, int num_splits, cudaStream_t stream) {
+  run_splitk(Q, K, V, output, po, pm, pl, batch_size, N_latent, N_input, dim, num_splits, stream);
+}
+
+extern "C" void launch_wmma_splitk_kernel(const __half* Q, const __half* K, const __half* V,
+                                          float* output, float* po, float* pm, float* pl,
+                                          int batch_size, int N_latent, int N_input, int dim,
+                                          int num_splits, cudaStream_t stream) {
+  if (bad_sizes(batch_size, N_latent, N_input, dim) || num_splits <= 0) {
+    set_error(XATTN_ERR_ARG);
+    return;
+  }
+  if (batch_size == 0 || N_latent == 0) { set_error(XATTN_OK); return; }
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) { set_error(rc); return; }
+  // Chunk rounded up to a multiple of 16 keys (kernel_wmma_splitk.cu:52).
+  const int chunk = std::max(16, ((N_input + num_splits - 1) / num_splits + 15) / 16 * 16);
+  rc = launch_simt<__half, float>(Q, K, V, nullptr, po, pm, pl, batch_size, 1, N_latent, N_input,
+                                  dim, num_splits, chunk, 1, kLog2e, stream);
+  if (rc != XATTN_OK) { set_error(rc); return; }
+  set_error(launch_combine(po, pm, pl, output, static_cast<long long>(batch_size) * N_latent, dim,
+                           num_splits, stream));
+}
+
+// ===================================================================== Part 2: new API
+extern "C" int xattn_fp32(const float* Q, const float* K, const float* V, float* output,
+                          int batch_size, int N_latent, int N_input, int dim,
+                          cudaStream_t stream) {
+  return run_fp32(Q, K, V, output, batch_size, N_latent, N_input, dim, stream);
+}
+
+extern "C" int xattn_fp32_partial(const float* Q, const float* K, const float* V, float* po,
+                                  float* pm, float* pl, int batch_size, int N_latent,
+                                  int N_input, int dim, cudaStream_t stream) {
+  if (bad_sizes(batch_size, N_latent, N_input, dim)) return set_error(XATTN_ERR_ARG);
+  if (batch_size == 0 || N_latent == 0) return set_error(XATTN_OK);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return set_error(rc);
+  const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(dim));
+  const int chunk = std::max(1, N_input);
+  if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, po, dim))
+    return set_error(launch_simt<float, float>(Q, K, V, nullptr, po, pm, pl, batch_size, 1, N_latent,
+                                               N_input, dim, 1, chunk, 1, scale_log2, stream));
+  return set_error(launch_fused(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim, 1,
+                                chunk, 1, stream));
+}
+
+extern "C" int xattn_combine(const float* po, const float* pm, const float* pl, float* output,
+                             long long rows, int dim, int num_splits, cudaStream_t stream) {
+  if (rows < 0 || dim <= 0 || num_splits <= 0) return set_error(XATTN_ERR_ARG);
+  return set_error(launch_combine(po, pm, pl, output, rows, dim, num_splits, stream));
+}
+
+extern "C" int xattn_lse_pack(const float* po, const float* pl, float* ol, long long rows, int dim,
+                              cudaStream_t stream) {
+  if (rows < 0 || dim <= 0) return set_error(XATTN_ERR_ARG);
+  if (rows == 0) return set_error(XATTN_OK);
+  simt::lse_pack_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, stream>>>(po, pl, ol, rows,
+                                                                                    dim);
+  return set_error(cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+}
+
+extern "C" int xattn_lse_rescale(float* ol, const float* pm, const float* m_glob, long long rows,
+                                 int dim, cudaStream_t stream) {
+  if (rows < 0 || dim <= 0) return set_error(XATTN_ERR_ARG);
+  if (rows == 0) return set_error(XATTN_OK);
+  simt::lse_rescale_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, stream>>>(ol, pm, m_glob,
+                                                                                       rows, dim);
+  return set_error(cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+}
+
+extern "C" int xattn_lse_finalize(const float* ol, float* output, long long rows, int dim,
+                                  cudaStream_t stream) {
+  if (rows < 0 || dim <= 0) return set_error(XATTN_ERR_ARG);
+  if (rows == 0) return set_error(XATTN_OK);
+  simt::lse_finalize_kernel<<<static_cast<unsigned>((rows + 3) / 4), 128, 0, stream>>>(ol, output,
+                                                                                        rows, dim);
+  return set_error(cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+}
+
+extern "C" int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K,
+                              const __nv_bfloat16* V, __nv_bfloat16* output, int batch_size,
+                              int N_latent, int N_input, int heads, int head_dim,
+                              cudaStream_t stream) {
+  if (bad_sizes(batch_size, N_latent, N_input, head_dim) || heads <= 0)
+    return set_error(XATTN_ERR_ARG);
+  if (batch_size == 0 || N_latent == 0 || N_input == 0) return set_error(XATTN_OK);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return set_error(rc);
+  const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(head_dim));
+  return set_error(launch_simt<__nv_bfloat16, __nv_bfloat16>(
+      Q, K, V, output, nullptr, nullptr, nullptr, batch_size, heads, N_latent, N_input, head_dim, 1,
+      N_input, 0, scale_log2, stream));
+}
+
+extern "C" int xattn_plan_fp32(int batch_size, int N_latent, int N_input, int dim,
+                               int* num_splits) {
+  int splits = 1, chunk = N_input;
+  int launches = 0;
+  if (batch_size > 0 && N_latent > 0 && N_input > 0 && dim > 0) {
+    int dev = 0;
+    if (prepare_device(&dev) != XATTN_OK) return -1;
+    const bool tc = dim >= 64 && dim <= 2 * fused::kMaxDh && dim % 64 == 0 && g_opt_path.load() != 2;
+    if (tc) plan_splits(dev, batch_size, N_latent, N_input, g_opt_path.load(), &splits, &chunk);
+    launches = splits > 1 ? 2 : 1;
+  } else if (batch_size > 0 && N_latent > 0 && N_input == 0) {
+    launches = 1;  // the zero fill
+  }
+  if (num_splits != nullptr) *num_splits = splits;
+  return launches;
+}
+
+extern "C" int xattn_last_error(void) { return t_last_error; }
+
+extern "C" int xattn_status(int clear) {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  int st = 0;
+  if (cudaMemcpyFromSymbol(&st, g_status, sizeof(int)) != cudaSuccess) return -1;
+  if (clear) {
+    const int zero = 0;
+    cudaMemcpyToSymbol(g_status, &zero, sizeof(int));
+  }
+  return st;
+}
+
+extern "C" int xattn_set_option(int key, int value) {
+  switch (key) {
+    case 1: return g_opt_path.exchange(value);
+    case 2: return g_opt_splits.exchange(value);
+    case 3: return g_opt_wait_us.exchange(value > 0 ? value : 2000000);
+    case 4: return g_opt_tf32_comp.exchange(value);
+    default: return -1;
+  }
+}
+
+namespace xattn {
+namespace {
+// Waits on an mbarrier that is initialised with one expected arrival that never comes.
+__global__ void selftest_timeout_kernel() {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bar), 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!mbar_wait(smem_u32(&bar), 0, kTimeoutInjected, &abort_flag)) {
+      // give-up path taken: status already recorded by mbar_wait
+    }
+  }
+  __syncthreads();
+}
+}  // namespace
+}  // namespace xattn
+
+extern "C" int xattn_selftest_timeout(int bound_us) {
+  const int prev = g_opt_wait_us.exchange(bound_us > 0 ? bound_us : 1000);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  int st = -1;
+  if (rc == XATTN_OK) {
+    selftest_timeout_kernel<<<1, 32>>>();
+    st = xattn_status(1);
+  }
+  g_opt_wait_us.store(prev);
+  prepare_device(&dev);
+  return st;
+}
+
+extern "C" int xattn_version(void) { return kVersion; }

@@ -1,0 +1,285 @@
+"""PyTorch-facing API of the B200 cross-attention library (``kernels.so``).
+
+Functions take CUDA tensors and launch on ``torch.cuda.current_stream()``:
+
+* ``cross_attention(q, k, v)``          fp32 API, O = softmax(q k^T / sqrt(D)) v
+  (the upstream ``compute_cross_attention`` contract, ``generate_batch_references.py:20-26``);
+* ``cross_attention_splitk(q, k, v, num_splits)``  the upstream split-K entry with
+  caller-visible (m, l, O) partials (``kernel_splitk.cu:42-251``);
+* ``cross_attention_partial`` / ``combine``        partial triples and their merge;
+* ``cross_attention_bf16_mha(q, k, v, heads)``     multi-head bf16 (no upstream counterpart).
+
+Multi-GPU (one process per GPU, ``torch.distributed``):
+
+* ``shard_rows`` -- batch rows split contiguously over ranks; every rank runs the
+  fused kernel on its own shard, no collective on the data path (weak scaling).
+* ``cross_attention_input_split`` -- N_input split over ranks: each rank computes the
+  partial (m, l, O) of its key slice, then ``merge_input_split`` does
+  all-reduce(MAX, m) -> rescale -> all-reduce(SUM, [O | l]) -> O / l over NCCL.
+
+Roofline formulas follow ``experiments/roofline.py:25-36`` upstream:
+FLOPs = 4 B Nl Ni D, fused bytes = (2 Nl D + 2 Ni D) B elem.
+
+The library must be built (``make`` in this directory); importing this module on a
+machine without it raises, there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+from typing import Callable, Optional, Sequence
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("XATTN_LIB", os.path.join(_HERE, "kernels.so"))
+
+_lib = None
+
+# Names every build of kernels.so exports (the contract of include/xattn.h).
+EXPORTED = (
+    "launch_naive_kernel", "launch_parallel_kernel", "launch_tiled_kernel",
+    "launch_optimized_kernel", "launch_wmma_kernel", "launch_splitk_kernel",
+    "launch_wmma_splitk_kernel", "xattn_fp32", "xattn_fp32_partial", "xattn_combine",
+    "xattn_lse_pack", "xattn_lse_rescale", "xattn_lse_finalize", "xattn_bf16_mha",
+    "xattn_last_error", "xattn_status", "xattn_set_option", "xattn_selftest_timeout",
+    "xattn_version", "xattn_plan_fp32",
+)
+
+OPT_PATH, OPT_SPLITS, OPT_WAIT_US, OPT_TF32_COMP = 1, 2, 3, 4
+
+
+def lib():
+    """Load kernels.so once and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} not found: build it with `make -C {_HERE}`")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, i, ll = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    sig = {
+        "launch_naive_kernel": ([vp] * 4 + [i] * 4 + [vp], None),
+        "launch_parallel_kernel": ([vp] * 4 + [i] * 4 + [vp], None),
+        "launch_tiled_kernel": ([vp] * 4 + [i] * 4 + [vp], None),
+        "launch_optimized_kernel": ([vp] * 4 + [i] * 4 + [vp], None),
+        "launch_wmma_kernel": ([vp] * 4 + [i] * 4 + [vp], None),
+        "launch_splitk_kernel": ([vp] * 7 + [i] * 5 + [vp], None),
+        "launch_wmma_splitk_kernel": ([vp] * 7 + [i] * 5 + [vp], None),
+        "xattn_fp32": ([vp] * 4 + [i] * 4 + [vp], i),
+        "xattn_fp32_partial": ([vp] * 6 + [i] * 4 + [vp], i),
+        "xattn_combine": ([vp] * 4 + [ll, i, i, vp], i),
+        "xattn_lse_pack": ([vp] * 3 + [ll, i, vp], i),
+        "xattn_lse_rescale": ([vp] * 3 + [ll, i, vp], i),
+        "xattn_lse_finalize": ([vp] * 2 + [ll, i, vp], i),
+        "xattn_bf16_mha": ([vp] * 4 + [i] * 5 + [vp], i),
+        "xattn_last_error": ([], i),
+        "xattn_status": ([i], i),
+        "xattn_set_option": ([i, i], i),
+        "xattn_selftest_timeout": ([i], i),
+        "xattn_version": ([], i),
+        "xattn_plan_fp32": ([i, i, i, i, ctypes.POINTER(i)], i),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(L, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = L
+    return L
+
+
+def set_option(key: int, value: int) -> int:
+    return lib().xattn_set_option(key, value)
+
+
+def plan_fp32(b: int, nl: int, ni: int, d: int):
+    """(kernel launches per call, key splits) the fp32 entry will use for this shape."""
+    n = ctypes.c_int(0)
+    launches = lib().xattn_plan_fp32(b, nl, ni, d, ctypes.byref(n))
+    return launches, n.value
+
+
+def device_status(clear: bool = True) -> int:
+    return lib().xattn_status(1 if clear else 0)
+
+
+# ----------------------------------------------------------------------------- roofline
+def flops(b: int, nl: int, ni: int, d: int) -> float:
+    """Forward FLOPs of the two matmuls, 4 B Nl Ni D (upstream roofline.py:25-27)."""
+    return 4.0 * b * nl * ni * d
+
+
+def bytes_moved(b: int, nl: int, ni: int, d: int, elem: int = 4) -> float:
+    """Fused HBM bytes, (2 Nl D + 2 Ni D) B elem (upstream roofline.py:30-36)."""
+    return (2.0 * nl * d + 2.0 * ni * d) * b * elem
+
+
+# ----------------------------------------------------------------------------- helpers
+def _stream():
+    import torch
+
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _as3(x):
+    return x.unsqueeze(0) if x.dim() == 2 else x
+
+
+def _check_fp32(*ts):
+    import torch
+
+    for t in ts:
+        if not t.is_cuda or t.dtype != torch.float32 or not t.is_contiguous():
+            raise ValueError("expected contiguous float32 CUDA tensors")
+
+
+def _raise(rc: int, what: str):
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with xattn status {rc}")
+
+
+# ----------------------------------------------------------------------------- single GPU
+def cross_attention(q, k, v, out=None):
+    """O = softmax(q k^T / sqrt(D)) v on the GPU (tcgen05 TF32 with fp32 accumulation)."""
+    import torch
+
+    squeeze = q.dim() == 2
+    q, k, v = _as3(q), _as3(k), _as3(v)
+    _check_fp32(q, k, v)
+    b, nl, d = q.shape
+    ni = k.shape[1]
+    if out is None:
+        out = torch.empty_like(q)
+    _raise(lib().xattn_fp32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni,
+                            d, _stream()), "xattn_fp32")
+    return out[0] if squeeze else out
+
+
+def cross_attention_splitk(q, k, v, num_splits: int):
+    """Upstream split-K entry: returns (out, po, pm, pl) with the upstream scratch layout."""
+    import torch
+
+    q, k, v = _as3(q), _as3(k), _as3(v)
+    _check_fp32(q, k, v)
+    b, nl, d = q.shape
+    ni = k.shape[1]
+    out = torch.empty_like(q)
+    po = torch.empty(b, nl, num_splits, d, device=q.device, dtype=torch.float32)
+    pm = torch.empty(b, nl, num_splits, device=q.device, dtype=torch.float32)
+    pl = torch.empty_like(pm)
+    L = lib()
+    L.launch_splitk_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), po.data_ptr(),
+                           pm.data_ptr(), pl.data_ptr(), b, nl, ni, d, num_splits, _stream())
+    _raise(L.xattn_last_error(), "launch_splitk_kernel")
+    return out, po, pm, pl
+
+
+def cross_attention_partial(q, k, v):
+    """Partial (m, l, O) of the keys in k/v: po [B,Nl,D], pm, pl [B,Nl] (natural-log units)."""
+    import torch
+
+    q, k, v = _as3(q), _as3(k), _as3(v)
+    _check_fp32(q, k, v)
+    b, nl, d = q.shape
+    ni = k.shape[1]
+    po = torch.empty_like(q)
+    pm = torch.empty(b, nl, device=q.device, dtype=torch.float32)
+    pl = torch.empty_like(pm)
+    _raise(lib().xattn_fp32_partial(q.data_ptr(), k.data_ptr(), v.data_ptr(), po.data_ptr(),
+                                    pm.data_ptr(), pl.data_ptr(), b, nl, ni, d, _stream()),
+           "xattn_fp32_partial")
+    return po, pm, pl
+
+
+def combine(po, pm, pl):
+    """Merge [..., S, D] partials into [..., D] (upstream kernel_splitk.cu:186-236)."""
+    import torch
+
+    s, d = po.shape[-2], po.shape[-1]
+    rows = po.numel() // (s * d)
+    out = torch.empty(po.shape[:-2] + (d,), device=po.device, dtype=torch.float32)
+    _raise(lib().xattn_combine(po.data_ptr(), pm.data_ptr(), pl.data_ptr(), out.data_ptr(), rows, d,
+                               s, _stream()), "xattn_combine")
+    return out
+
+
+def cross_attention_bf16_mha(q, k, v, heads: int, out=None):
+    """Multi-head bf16 attention: [B,N,H*dh] inputs, heads contiguous, scale 1/sqrt(dh)."""
+    import torch
+
+    b, nl, dm = q.shape
+    ni = k.shape[1]
+    if dm % heads:
+        raise ValueError("model width must be a multiple of heads")
+    for t in (q, k, v):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError("expected contiguous bfloat16 CUDA tensors")
+    if out is None:
+        out = torch.empty_like(q)
+    _raise(lib().xattn_bf16_mha(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni,
+                                heads, dm // heads, _stream()), "xattn_bf16_mha")
+    return out
+
+
+# ----------------------------------------------------------------------------- multi-GPU
+def shard_rows(total: int, rank: int, world: int):
+    """Contiguous [begin, end) slice of `total` items for `rank` of `world` (balanced)."""
+    base, extra = divmod(total, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+class MergeOps:
+    """The three device steps of the N_input merge; the default binds the CUDA kernels."""
+
+    def pack(self, po, pl):
+        import torch
+
+        rows, d = pl.numel(), po.shape[-1]
+        ol = torch.empty(rows, d + 1, device=po.device, dtype=torch.float32)
+        _raise(lib().xattn_lse_pack(po.data_ptr(), pl.data_ptr(), ol.data_ptr(), rows, d, _stream()),
+               "xattn_lse_pack")
+        return ol
+
+    def rescale(self, ol, pm, m_glob):
+        _raise(lib().xattn_lse_rescale(ol.data_ptr(), pm.data_ptr(), m_glob.data_ptr(), ol.shape[0],
+                                       ol.shape[1] - 1, _stream()), "xattn_lse_rescale")
+        return ol
+
+    def finalize(self, ol):
+        import torch
+
+        rows, d = ol.shape[0], ol.shape[1] - 1
+        out = torch.empty(rows, d, device=ol.device, dtype=torch.float32)
+        _raise(lib().xattn_lse_finalize(ol.data_ptr(), out.data_ptr(), rows, d, _stream()),
+               "xattn_lse_finalize")
+        return out
+
+
+def merge_input_split(po, pm, pl, group=None, ops: Optional[MergeOps] = None):
+    """Merge per-rank partials of disjoint key slices into the full attention output.
+
+    Collective protocol (identical on every rank, same order):
+      1. m_glob = all_reduce(MAX, pm)                     [rows] fp32
+      2. ol = [po | pl] rescaled by exp(pm - m_glob)       local
+      3. all_reduce(SUM, ol)                               [rows, D+1] fp32
+      4. out = ol[:, :D] / ol[:, D]                         local
+    Returns out with po's shape.
+    """
+    import torch.distributed as dist
+
+    ops = ops or MergeOps()
+    shape = po.shape
+    pm_flat = pm.reshape(-1).contiguous()
+    m_glob = pm_flat.clone()
+    dist.all_reduce(m_glob, op=dist.ReduceOp.MAX, group=group)
+    ol = ops.pack(po.reshape(-1, shape[-1]).contiguous(), pl.reshape(-1).contiguous())
+    ol = ops.rescale(ol, pm_flat, m_glob)
+    dist.all_reduce(ol, op=dist.ReduceOp.SUM, group=group)
+    return ops.finalize(ol).reshape(shape)
+
+
+def cross_attention_input_split(q, k_local, v_local, group=None):
+    """Attention over the union of every rank's key slice (N_input split across GPUs)."""
+    po, pm, pl = cross_attention_partial(q, k_local, v_local)
+    return merge_input_split(po, pm, pl, group)

@@ -1,0 +1,162 @@
+/*
+ * xattn.h -- C ABI of the B200 (sm_100a) cross-attention library `kernels.so`.
+ *
+ * O = softmax(Q K^T / sqrt(D)) V for Q[B][N_latent][D], K,V[B][N_input][D], row-major,
+ * contiguous, device pointers owned by the caller.  Every launch is asynchronous on
+ * `stream` (NULL = legacy default stream) and runs on the current device.
+ *
+ * Part 1 repeats, symbol for symbol and argument for argument, the entry points the
+ * upstream project's ctypes wrapper binds (satyam19k/fast-cuda-cross-attention,
+ * cuda_wrappers.py:83-175), so that project's cuda_wrappers.py, benchmark.py and
+ * benchmark_batching.py load this library unchanged.  Like upstream they return void;
+ * launch errors surface through cudaGetLastError() of the shared CUDA runtime (the
+ * library links libcudart dynamically), and host-side argument errors through
+ * xattn_last_error().
+ *
+ * Part 2 is new API: status-returning variants, caller-owned split partials, the bf16
+ * multi-head entry, the pieces of the multi-GPU N_input merge, and diagnostics.
+ */
+#ifndef XATTN_H_
+#define XATTN_H_
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- Part 1: upstream ABI */
+
+/* Replaces launch_naive_kernel (kernel_naive.cu:68-89; bound at cuda_wrappers.py:83-94).
+ * Same result as launch_optimized_kernel: all four fp32 names share one kernel family.  */
+void launch_naive_kernel(const float* Q, const float* K, const float* V, float* output,
+                         int batch_size, int N_latent, int N_input, int dim,
+                         cudaStream_t stream);
+
+/* Replaces launch_parallel_kernel (kernel_warp_parallel.cu:113-139; cuda_wrappers.py:96-107).
+ * No shared-memory design limit: any N_input is accepted.                               */
+void launch_parallel_kernel(const float* Q, const float* K, const float* V, float* output,
+                            int batch_size, int N_latent, int N_input, int dim,
+                            cudaStream_t stream);
+
+/* Replaces launch_tiled_kernel (kernel_tiled.cu:169-186; cuda_wrappers.py:109-120).     */
+void launch_tiled_kernel(const float* Q, const float* K, const float* V, float* output,
+                         int batch_size, int N_latent, int N_input, int dim,
+                         cudaStream_t stream);
+
+/* Replaces launch_optimized_kernel (kernel_vectorized.cu:198-215; cuda_wrappers.py:122-133).
+ * fp32 in/out, tcgen05 kind::tf32 tensor cores with fp32 accumulation; picks a key split
+ * on its own when batch_size * N_latent is too small to fill the GPU (library-owned
+ * workspace, allocated once per device and stream and grown on demand).                */
+void launch_optimized_kernel(const float* Q, const float* K, const float* V, float* output,
+                             int batch_size, int N_latent, int N_input, int dim,
+                             cudaStream_t stream);
+
+/* Replaces launch_wmma_kernel (kernel_wmma.cu:139-154; cuda_wrappers.py:136-146).
+ * fp16 Q (already multiplied by 1/sqrt(dim) by the caller, cuda_wrappers.py:635-640),
+ * fp16 K, V; fp32 output.  Any N_latent / N_input (upstream needs multiples of 16).     */
+void launch_wmma_kernel(const __half* Q, const __half* K, const __half* V, float* output,
+                        int batch_size, int N_latent, int N_input, int dim,
+                        cudaStream_t stream);
+
+/* Replaces launch_splitk_kernel (kernel_splitk.cu:238-251; cuda_wrappers.py:149-161).
+ * Split s covers keys [s*c, min((s+1)*c, N_input)) with c = ceil(N_input/num_splits)
+ * (kernel_splitk.cu:59-61).  Caller-owned scratch in the upstream layout:
+ *   po [B][N_latent][num_splits][dim], pm, pl [B][N_latent][num_splits]  (fp32)
+ * pm = max scaled score of the split (natural-log units), pl = sum exp(s - pm),
+ * po = sum exp(s - pm) v; empty splits hold pm = -FLT_MAX, pl = 0, po = 0.
+ * The merge divides by L exactly (upstream adds 1e-6, kernel_splitk.cu:225).           */
+void launch_splitk_kernel(const float* Q, const float* K, const float* V, float* output,
+                          float* po, float* pm, float* pl, int batch_size, int N_latent,
+                          int N_input, int dim, int num_splits, cudaStream_t stream);
+
+/* Replaces launch_wmma_splitk_kernel (kernel_wmma_splitk.cu:201-219; cuda_wrappers.py:164-175).
+ * fp16 inputs as launch_wmma_kernel; split chunk rounded up to a multiple of 16 keys
+ * (kernel_wmma_splitk.cu:52); scratch layout as launch_splitk_kernel.                  */
+void launch_wmma_splitk_kernel(const __half* Q, const __half* K, const __half* V,
+                               float* output, float* po, float* pm, float* pl, int batch_size,
+                               int N_latent, int N_input, int dim, int num_splits,
+                               cudaStream_t stream);
+
+/* ---------------------------------------------------------------- Part 2: new API */
+
+/* Status codes returned by the xattn_* functions and by xattn_last_error(). */
+#define XATTN_OK 0
+#define XATTN_ERR_ARG 1        /* negative size, null pointer, bad alignment           */
+#define XATTN_ERR_LAUNCH 2     /* a kernel launch failed (see cudaGetLastError)         */
+#define XATTN_ERR_NOMEM 3      /* the library workspace could not be grown              */
+#define XATTN_ERR_DEVICE 4     /* a device wait timed out (see xattn_status)            */
+
+/* Status-returning form of launch_optimized_kernel (no counterpart upstream).          */
+int xattn_fp32(const float* Q, const float* K, const float* V, float* output, int batch_size,
+               int N_latent, int N_input, int dim, cudaStream_t stream);
+
+/* Unnormalised partial (m, l, O) of the keys this call sees, written with num_splits = 1
+ * in the launch_splitk_kernel layout: po [B][N_latent][dim], pm, pl [B][N_latent].
+ * Building block of the multi-GPU N_input split (no counterpart upstream).              */
+int xattn_fp32_partial(const float* Q, const float* K, const float* V, float* po, float* pm,
+                       float* pl, int batch_size, int N_latent, int N_input, int dim,
+                       cudaStream_t stream);
+
+/* Log-sum-exp merge of split partials into output (the combine half of
+ * launch_splitk_kernel, kernel_splitk.cu:186-236), rows = B * N_latent.                 */
+int xattn_combine(const float* po, const float* pm, const float* pl, float* output,
+                  long long rows, int dim, int num_splits, cudaStream_t stream);
+
+/* Multi-GPU N_input split merge, run on every rank between NCCL collectives:
+ *   pack:     ol[r] = [po[r][0..dim), pl[r]]                     ([rows][dim+1] fp32)
+ *   (all-reduce MAX of pm -> m_glob)
+ *   rescale:  ol[r] *= exp(pm[r] - m_glob[r])
+ *   (all-reduce SUM of ol)
+ *   finalize: output[r] = ol[r][0..dim) / ol[r][dim]                                    */
+int xattn_lse_pack(const float* po, const float* pl, float* ol, long long rows, int dim,
+                   cudaStream_t stream);
+int xattn_lse_rescale(float* ol, const float* pm, const float* m_glob, long long rows, int dim,
+                      cudaStream_t stream);
+int xattn_lse_finalize(const float* ol, float* output, long long rows, int dim,
+                       cudaStream_t stream);
+
+/* Multi-head bf16 cross attention (no counterpart upstream): Q [B][N_latent][H*dh],
+ * K, V [B][N_input][H*dh], heads contiguous inside each row, per-head scale 1/sqrt(dh),
+ * fp32 accumulation, bf16 output [B][N_latent][H*dh].                                  */
+int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                   __nv_bfloat16* output, int batch_size, int N_latent, int N_input,
+                   int heads, int head_dim, cudaStream_t stream);
+
+/* Plan of an xattn_fp32 / launch_optimized_kernel call on the current device for aligned
+ * pointers: returns the number of kernels the call launches (1, or 2 with a key split
+ * and its merge) and stores the key-split count in *num_splits (may be NULL).          */
+int xattn_plan_fp32(int batch_size, int N_latent, int N_input, int dim, int* num_splits);
+
+/* Host-side status of the most recent call on this thread (XATTN_* code).              */
+int xattn_last_error(void);
+
+/* Device status word: 0, or the code of the first bounded device wait that gave up.
+ * Synchronises the current device.  clear != 0 resets it to 0.                          */
+int xattn_status(int clear);
+
+/* Options for tests and tuning.  key 1 = path: 0 auto, 1 tensor-core kernels only
+ * (no automatic key split), 2 CUDA-core generic kernel.  key 2 = forced number of key
+ * splits for the automatic fp32 path (0 = heuristic).  key 3 = device wait bound in
+ * microseconds (default 2,000,000).  key 4 = TF32 truncation-bias compensation of the
+ * tensor-core fp32 path: 1 (default) scales scores by (1 + 2e) and the output by (1 + e),
+ * e = 2^-11 / (2 ln 2), the mean relative truncation error of one operand; 0 turns it
+ * off (for inputs already exact in TF32).  Returns the previous value.                 */
+int xattn_set_option(int key, int value);
+
+/* Runs a kernel that waits on an mbarrier nothing will ever arrive on, with the wait
+ * bound set to `bound_us`; returns the device status it produced (expected: the
+ * injected-timeout code 99) and clears it.  Exercises the give-up path of every
+ * bounded wait without faulting or hanging the GPU.                                    */
+int xattn_selftest_timeout(int bound_us);
+
+/* Library version: major * 10000 + minor * 100 + patch.                               */
+int xattn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* XATTN_H_ */

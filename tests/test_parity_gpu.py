@@ -1,0 +1,311 @@
+"""GPU parity of every entry point against the oracle, the golden fixtures and a torch
+fp32 reference (run on a B200 with ``-m gpu``).
+
+Tolerances (written per test):
+  * TF32 fp32 API:      max|dO| <= 2e-3 * max|O_ref|   (plus the upstream drivers'
+                        1e-3 absolute, benchmark.py:174-202, on the seeded configs)
+  * fp16 entries:       max|dO| <= 2e-3 * max|O_ref| against the fp16-rounded inputs
+  * bf16 multi-head:    max|dO| <= 2e-2 * max|O_ref| against the bf16-rounded inputs
+Every output buffer is surrounded by NaN sentinels that must survive the call.
+"""
+
+import math
+import os
+
+import numpy as np
+import pytest
+
+import xattn_oracle as orc
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 2e-3
+D768 = 768
+
+
+@pytest.fixture(scope="module")
+def torch_cuda():
+    import torch
+
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    return torch
+
+
+@pytest.fixture(scope="module")
+def X():
+    import xattn
+
+    xattn.lib()
+    yield xattn
+    assert xattn.device_status() == 0
+
+
+def ref_attention(torch, q, k, v, scale=None):
+    q, k, v = q.double(), k.double(), v.double()
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    return (torch.softmax(q @ k.transpose(-1, -2) * scale, -1) @ v).float()
+
+
+def guarded_empty(torch, shape, dtype):
+    """Output tensor inside a NaN-filled guard region; returns (view, checker)."""
+    n = int(np.prod(shape))
+    pad = 4096
+    buf = torch.full((n + 2 * pad,), float("nan"), device="cuda", dtype=dtype)
+    view = buf[pad:pad + n].view(shape)
+
+    def intact():
+        return bool(torch.isnan(buf[:pad].float()).all()) and bool(torch.isnan(buf[pad + n:].float()).all())
+
+    return view, intact
+
+
+def assert_close(torch, out, ref, tol, what):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item()
+    assert math.isfinite(err), f"{what}: non-finite output"
+    assert err <= tol * scale, f"{what}: max|dO| {err:.3e} > {tol} * {scale:.3e}"
+    return err
+
+
+# ----------------------------------------------------------------------- golden (upstream data)
+@pytest.mark.parametrize("nl", [64, 128, 256, 512, 1024])
+def test_golden_single_batch_through_upstream_api(X, nl):
+    """generate_references.py data through run_vectorized_kernel (host arrays in/out)."""
+    import cuda_wrappers as cw
+
+    g = np.load(os.path.join(GOLDEN, "golden_single.npz"))
+    q, k, v = orc.seeded_inputs_single(nl, 784, D768)
+    out = cw.run_vectorized_kernel(q, k, v, nl, 784, D768)
+    flat = out.reshape(-1, D768)
+    rows, vals = g[f"nl{nl}/rows"], g[f"nl{nl}/row_vals"]
+    scale = float(g[f"nl{nl}/row_absmax"].max())
+    err = np.abs(flat[rows] - vals).max()
+    assert err <= TF32_TOL * scale and err <= 1e-3, err
+    row_sum_err = np.abs(flat.sum(1, dtype=np.float64) - g[f"nl{nl}/row_sum"]).max()
+    assert row_sum_err <= TF32_TOL * scale * D768
+
+
+@pytest.mark.parametrize("b,nl", [(4, 64), (8, 512), (16, 128), (32, 1024)])
+def test_golden_batches(X, torch_cuda, b, nl):
+    """generate_batch_references.py data, incl. the headline B=32 Nl=1024 config."""
+    torch = torch_cuda
+    g = np.load(os.path.join(GOLDEN, "golden_batch.npz"))
+    key = f"b{b}_nl{nl}"
+    q, k, v = orc.seeded_inputs_batch(b, nl, 784, D768)
+    assert orc.sha256(q) == str(g[f"{key}/sha_q"])
+    tq, tk, tv = (torch.from_numpy(x).cuda() for x in (q, k, v))
+    out = X.cross_attention(tq, tk, tv)
+    flat = out.reshape(-1, D768).cpu().numpy()
+    rows, vals = g[f"{key}/rows"], g[f"{key}/row_vals"]
+    scale = float(g[f"{key}/row_absmax"].max())
+    err = np.abs(flat[rows] - vals).max()
+    assert err <= TF32_TOL * scale and err <= 1e-3, err
+    # size-independent checks over every row: row sums and row abs-max
+    assert np.abs(flat.sum(1, dtype=np.float64) - g[f"{key}/row_sum"]).max() <= TF32_TOL * scale * 50
+    assert np.abs(np.abs(flat).max(1) - g[f"{key}/row_absmax"]).max() <= TF32_TOL * scale
+    # full tensor against a double-precision torch reference on the GPU
+    assert_close(torch, out, ref_attention(torch, tq, tk, tv), TF32_TOL, key)
+
+
+def test_golden_perceiver_long_input(X, torch_cuda):
+    torch = torch_cuda
+    g = np.load(os.path.join(GOLDEN, "golden_perceiver.npz"))
+    q, k, v = orc.seeded_inputs_perceiver(64, 12544)
+    out = X.cross_attention(*(torch.from_numpy(x).cuda() for x in (q, k, v))).cpu().numpy()
+    rows, vals = g["nl64_ni12544/rows"], g["nl64_ni12544/row_vals"]
+    scale = float(g["nl64_ni12544/row_absmax"].max())
+    assert np.abs(out[rows] - vals).max() <= TF32_TOL * scale
+
+
+# ----------------------------------------------------------------------- fp32 API shapes
+SHAPES = [
+    # (B, Nl, Ni, D) tensor-core path: D multiple of 64 up to 768
+    (1, 1, 1, 768), (1, 64, 784, 768), (2, 128, 256, 768), (3, 200, 300, 128),
+    (2, 257, 1000, 512), (4, 130, 129, 64), (1, 127, 17, 256), (2, 129, 16, 768),
+    (1, 300, 2049, 384),
+    # generic path: D outside the tensor-core set
+    (2, 100, 50, 96), (1, 33, 70, 32), (2, 17, 40, 1024), (1, 5, 9, 100),
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "B%d_Nl%d_Ni%d_D%d" % s)
+def test_fp32_shapes_with_guards(X, torch_cuda, shape):
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    gen = torch.Generator(device="cuda").manual_seed(sum(shape))
+    q = torch.randn(b, nl, d, device="cuda", generator=gen)
+    k = torch.randn(b, ni, d, device="cuda", generator=gen)
+    v = torch.randn(b, ni, d, device="cuda", generator=gen)
+    out, intact = guarded_empty(torch, (b, nl, d), torch.float32)
+    X.cross_attention(q, k, v, out=out)
+    torch.cuda.synchronize()
+    assert intact(), "write outside the output tensor"
+    assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, str(shape))
+
+
+def test_all_upstream_fp32_names_agree(X, torch_cuda):
+    torch = torch_cuda
+    L = X.lib()
+    q = torch.randn(2, 96, 768, device="cuda")
+    k = torch.randn(2, 300, 768, device="cuda")
+    v = torch.randn(2, 300, 768, device="cuda")
+    outs = []
+    for name in ("launch_naive_kernel", "launch_parallel_kernel", "launch_tiled_kernel",
+                 "launch_optimized_kernel"):
+        o = torch.zeros_like(q)
+        getattr(L, name)(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 2, 96, 300, 768, None)
+        outs.append(o)
+    torch.cuda.synchronize()
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert_close(torch, outs[0], ref_attention(torch, q, k, v), TF32_TOL, "names")
+
+
+def test_forced_paths_agree(X, torch_cuda):
+    """Automatic key split, forced single pass and the generic kernel give the same answer."""
+    torch = torch_cuda
+    q = torch.randn(1, 64, 768, device="cuda")
+    k = torch.randn(1, 784, 768, device="cuda")
+    v = torch.randn(1, 784, 768, device="cuda")
+    ref = ref_attention(torch, q, k, v)
+    results = {}
+    for label, key, val in (("auto", X.OPT_SPLITS, 0), ("one", X.OPT_SPLITS, 1),
+                            ("three", X.OPT_SPLITS, 3), ("generic", X.OPT_PATH, 2)):
+        prev = X.set_option(key, val)
+        try:
+            results[label] = X.cross_attention(q, k, v)
+            torch.cuda.synchronize()
+        finally:
+            X.set_option(key, prev)
+        assert_close(torch, results[label], ref, TF32_TOL, label)
+    assert (results["generic"] - ref).abs().max().item() < 1e-5
+
+
+def test_empty_and_degenerate_sizes(X, torch_cuda):
+    torch = torch_cuda
+    q = torch.randn(2, 5, 768, device="cuda")
+    k = torch.empty(2, 0, 768, device="cuda")
+    out = torch.full_like(q, 7.0)
+    X.cross_attention(q, k, k, out=out)  # softmax over no keys: zeros, as torch gives
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0
+    q0 = torch.empty(0, 5, 768, device="cuda")
+    X.cross_attention(q0, torch.randn(0, 3, 768, device="cuda"), torch.randn(0, 3, 768, device="cuda"))
+
+
+def test_batch_boundary_isolation(X, torch_cuda):
+    """Keys/rows of batch b+1 must never reach batch b (3-D TMA boxes clip per batch)."""
+    torch = torch_cuda
+    b, nl, ni, d = 2, 100, 200, 768
+    q = torch.randn(b, nl, d, device="cuda")
+    k = torch.randn(b, ni, d, device="cuda")
+    v = torch.randn(b, ni, d, device="cuda")
+    k[1].fill_(float("nan"))
+    v[1].fill_(float("nan"))
+    out = X.cross_attention(q, k, v)
+    torch.cuda.synchronize()
+    assert torch.isfinite(out[0]).all()
+    assert_close(torch, out[0:1], ref_attention(torch, q[0:1], k[0:1], v[0:1]), TF32_TOL, "batch0")
+
+
+def test_tf32_exact_inputs_without_compensation(X, torch_cuda):
+    torch = torch_cuda
+    q, k, v = (torch.randn(2, 128, 768, device="cuda") for _ in range(3))
+    q, k, v = (((x.view(torch.int32) + 0x1000) & -0x2000).view(torch.float32) for x in (q, k, v))
+    prev = X.set_option(X.OPT_TF32_COMP, 0)
+    try:
+        out = X.cross_attention(q, k, v)
+        torch.cuda.synchronize()
+    finally:
+        X.set_option(X.OPT_TF32_COMP, prev)
+    assert_close(torch, out, ref_attention(torch, q, k, v), 1e-3, "tf32-exact")
+
+
+# ----------------------------------------------------------------------- split-K entry
+@pytest.mark.parametrize("splits", [1, 3, 5, 37])
+def test_splitk_entry_and_partials(X, torch_cuda, splits):
+    torch = torch_cuda
+    b, nl, ni, d = 2, 130, 784, 768
+    q, k, v = (torch.randn(b, n, d, device="cuda") for n in (nl, ni, ni))
+    out, po, pm, pl = X.cross_attention_splitk(q, k, v, splits)
+    torch.cuda.synchronize()
+    assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, f"splitk{splits}")
+    # partial semantics (kernel_splitk.cu:42-181) against the oracle on a few rows
+    qs, ks, vs = (x[:, :8].cpu().numpy() if x is q else x.cpu().numpy() for x in (q, k, v))
+    rpo, rpm, rpl = orc.splitk_partials(qs, ks, vs, splits)
+    valid = rpm > -orc.FLT_MAX
+    gpm, gpl, gpo = pm[:, :8].cpu().numpy(), pl[:, :8].cpu().numpy(), po[:, :8].cpu().numpy()
+    assert np.all((gpm > -orc.FLT_MAX) == valid)
+    assert np.abs(gpm - rpm)[valid].max() <= 2e-3 * (1 + np.abs(rpm[valid]).max())
+    rel = np.abs(gpl - rpl)[valid] / rpl[valid]
+    assert rel.max() <= 1e-2
+    # empty splits hold (-FLT_MAX, 0, 0) as upstream
+    assert np.all(gpl[~valid] == 0) and np.all(gpo[~valid] == 0)
+
+
+# ----------------------------------------------------------------------- fp16 / bf16 entries
+def test_wmma_fp16_entries(X, torch_cuda):
+    import cuda_wrappers as cw
+
+    torch = torch_cuda
+    b, nl, ni, d = 2, 64, 784, 768
+    q, k, v = orc.seeded_inputs_batch(b, nl, ni, d)
+    out, _, _ = cw.benchmark_wmma_events(q, k, v, b, nl, ni, d, warmup=1, iters=2)
+    qh = torch.from_numpy((q / np.float32(np.sqrt(d))).astype(np.float16)).cuda()
+    kh, vh = (torch.from_numpy(x.astype(np.float16)).cuda() for x in (k, v))
+    ref = ref_attention(torch, qh, kh, vh, scale=1.0)
+    assert_close(torch, torch.from_numpy(out).cuda(), ref, TF32_TOL, "wmma")
+    out2, _, _, s = cw.benchmark_wmma_splitk_events(q, k, v, b, nl, ni, d, warmup=1, iters=2)
+    assert s >= 1
+    assert_close(torch, torch.from_numpy(out2).cuda(), ref, TF32_TOL, "wmma-splitk")
+
+
+@pytest.mark.parametrize("shape", [(2, 128, 200, 8, 96), (1, 33, 65, 4, 64), (32, 1024, 784, 8, 96)])
+def test_bf16_multihead(X, torch_cuda, shape):
+    torch = torch_cuda
+    b, nl, ni, h, dh = shape
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v = (torch.randn(b, n, h * dh, device="cuda", generator=gen).bfloat16() for n in (nl, ni, ni))
+    out, intact = guarded_empty(torch, (b, nl, h * dh), torch.bfloat16)
+    X.cross_attention_bf16_mha(q, k, v, h, out=out)
+    torch.cuda.synchronize()
+    assert intact()
+
+    def heads(x, n):
+        return x.float().view(b, n, h, dh).permute(0, 2, 1, 3)
+
+    ref = ref_attention(torch, heads(q, nl), heads(k, ni), heads(v, ni)).permute(0, 2, 1, 3)
+    assert_close(torch, out.float(), ref.reshape(b, nl, h * dh), 2e-2, f"bf16 {shape}")
+
+
+# ----------------------------------------------------------------------- multi-GPU pieces on one GPU
+def test_input_split_merge_kernels_single_gpu(X, torch_cuda):
+    """Partials of three key slices merged with the library's LSE kernels (the collectives
+    of the N_input split replaced by their single-process equivalents)."""
+    torch = torch_cuda
+    b, nl, ni, d = 2, 64, 900, 768
+    q, k, v = (torch.randn(b, n, d, device="cuda") for n in (nl, ni, ni))
+    parts = [X.cross_attention_partial(q, k[:, lo:hi].contiguous(), v[:, lo:hi].contiguous())
+             for lo, hi in ((0, 300), (300, 301), (301, 900))]
+    ops = X.MergeOps()
+    m_glob = torch.stack([pm.reshape(-1) for _, pm, _ in parts]).max(0).values
+    acc = None
+    for po, pm, pl in parts:
+        ol = ops.rescale(ops.pack(po.reshape(-1, d), pl.reshape(-1)), pm.reshape(-1).contiguous(), m_glob)
+        acc = ol.clone() if acc is None else acc + ol
+    out = ops.finalize(acc).view(b, nl, d)
+    torch.cuda.synchronize()
+    assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, "merge")
+
+
+# ----------------------------------------------------------------------- failure detection
+def test_bounded_wait_gives_up_cleanly(X, torch_cuda):
+    torch = torch_cuda
+    assert X.lib().xattn_selftest_timeout(1000) == 99
+    assert X.device_status() == 0
+    q = torch.randn(1, 8, 768, device="cuda")
+    out = X.cross_attention(q, q, q)  # the context is still usable afterwards
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all() and X.device_status() == 0
