@@ -13,13 +13,21 @@
 // Per key tile of 128 keys, each CTA:
 //   1. S_h = Q[:, half h] . K[tile, half h]^T      tcgen05 kind::tf32, SS, M=128 N=128,
 //      streaming 32-column chunks of Q and K through a TMA/mbarrier ring;
-//   2. exchanges S_h with its peer through distributed shared memory and forms
-//      S = S_0 + S_1 (identical bits in both CTAs: fp32 addition commutes);
-//   3. runs the online softmax on S in the log2 domain (scale log2(e)/sqrt(D) folded
-//      into one multiply), with lazy rescaling of O only when the running max grows by
-//      more than 2^8, rounds P to tf32 and writes it back over S in tensor memory;
-//   4. O_h += P . V[tile, half h]                    tcgen05 kind::tf32, TS (A = P in
-//      tensor memory), B = V streamed in 16-key chunks, MN-major 128B/32B-atom swizzle.
+//   2. softmax warps copy S_h out of tensor memory (which frees it for the next tile's
+//      Q.K^T) and send it to the peer CTA with st.async (distributed shared memory);
+//      S = S_0 + S_1 is formed in both CTAs (identical bits: fp32 addition commutes);
+//   3. online softmax in the log2 domain (scale log2(e)/sqrt(D) folded into one multiply)
+//      with lazy rescaling of O only when the running max grows by more than 2^8; P is
+//      rounded to tf32 and written, in place of the received scores, into shared memory
+//      in the UMMA K-major layout;
+//   4. O_h += P . V[tile, half h]                    tcgen05 kind::tf32, SS, B = V
+//      streamed in 16-key chunks, MN-major 128B swizzle with 32-byte atoms.
+// The MMA warp issues Q.K^T of tile j+1 before it waits for P of tile j, so the score
+// exchange and the softmax of one tile overlap the tensor-core work of the next.  Scores
+// never leave the chip.  After the last tile the epilogue divides by the row sum and
+// stores fp32 rows, or (split mode) stores the unnormalised partial (m, l, O) triple in
+// the upstream split-K scratch layout (kernel_splitk.cu:57: pidx = (b*Nl+row)*S+split).
+//
 // TF32 truncation bias.  kind::tf32 drops the low 13 mantissa bits of each fp32 operand
 // (truncation, measured on B200), which shrinks every operand by its relative truncation
 // error e.  For mantissas spread log-uniformly over an octave (Gaussian data, most real
@@ -29,13 +37,11 @@
 // output by (1 + E[e]) (out_comp), which removes the systematic part; the option can be
 // switched off for inputs that are already exactly representable in TF32.
 //
-// Scores never leave the chip.  After the last tile the epilogue divides by the row sum
-// and stores fp32 rows, or (split mode) stores the unnormalised partial (m, l, O) triple
-// in the upstream split-K scratch layout (kernel_splitk.cu:57: pidx = (b*Nl+row)*S+split).
-//
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer, warps 2..5 =
-// softmax / exchange / epilogue (warp w reads TMEM lanes 32*(w%4)..+31, i.e. one query
-// row per thread).  Every mbarrier wait is bounded (see sm100.cuh).
+// Warp roles (64 + 128 * kGroups threads): warp 0 = TMA producer, warp 1 = MMA issuer,
+// warps 2.. = softmax / exchange / epilogue.  Softmax warp w reads TMEM lanes
+// 32*(w%4)..+31 (one query row per thread) and column group (w-2)/4 of the score tile, so
+// each thread keeps its 64 scores in registers; row maxima and sums are combined across
+// the groups through shared memory.  Every mbarrier wait is bounded (sm100.cuh).
 #pragma once
 
 #include "sm100.cuh"
@@ -48,14 +54,23 @@ constexpr int kKeys = 128;          // keys per tile (UMMA N of Q.K^T)
 constexpr int kChunk = 32;          // fp32 columns per 128-byte swizzle row
 constexpr int kVKeys = 16;          // keys per V chunk
 constexpr int kStageBytes = 32768;  // Q chunk (16 KB) + K chunk (16 KB), or one V chunk
-constexpr int kStages = 4;
-constexpr int kSCol = 384;          // TMEM column of the S / P tile
+constexpr int kStages = 3;
+constexpr int kGroups = 2;                   // softmax column groups per TMEM lane quadrant
+constexpr int kGroupCols = kKeys / kGroups;  // score columns per softmax thread
+constexpr int kSoftmaxThreads = 128 * kGroups;
+constexpr int kSCol = 384;          // TMEM column of the S tile
 constexpr int kTmemCols = 512;
-constexpr int kXBytes = kRows * kKeys * 4;  // exchange buffer: one 128x128 fp32 tile
+constexpr int kXBytes = kRows * kKeys * 4;  // one exchange / P buffer: a 128x128 fp32 tile
+constexpr int kXBufs = 2;                   // double-buffered across key tiles
 constexpr int kMaxDh = 384;                 // D <= 768
-constexpr int kThreads = 192;
-constexpr int kSmemBytes = kStages * kStageBytes + kXBytes + 1024;
+constexpr int kThreads = 64 + kSoftmaxThreads;
+constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
 constexpr float kRescaleLog2 = 8.0f;        // lazy-rescale threshold (factor 256)
+// Static shared memory of the kernel (barriers, reduction arrays, slots), kept in the
+// budget check below together with the dynamic ring + exchange buffer.
+constexpr int kStaticSmemBytes = 1536;
+static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
+static_assert(kGroupCols == 64, "two 32-column register halves per softmax thread");
 
 struct Params {
   CUtensorMap tq;   // Q [B][Nl][D] fp32, box {32, 128, 1}, 128B swizzle
@@ -77,22 +92,31 @@ struct Params {
 struct __align__(8) Barriers {
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t s_full;   // MMA -> softmax: S tile ready
+  uint64_t s_full;   // MMA -> softmax: S tile ready in TMEM
+  uint64_t s_free;   // softmax -> MMA: S copied out of TMEM, columns reusable
   uint64_t p_full;   // softmax -> MMA: P (and any O rescale) ready
+  uint64_t pv_done[kXBufs];  // MMA -> softmax: P.V of a tile using buffer b complete
   uint64_t o_done;   // MMA -> epilogue: last P.V complete
-  uint64_t x_full;   // peer -> me: its partial scores are in my exchange buffer
-  uint64_t x_empty;  // peer -> me: it has drained its exchange buffer
+  uint64_t x_full[kXBufs];  // peer -> me: its partial scores are in my exchange buffer b
+  uint64_t x_empty;  // peer -> me: the peer's buffer for my next send may be refilled
   uint64_t drain;    // MMA issuer: everything it issued has completed
 };
-
-__device__ __forceinline__ uint32_t t_s_addr(uint32_t t_row, int c) {
-  return t_row + kSCol + c * 32;
-}
 
 __device__ __forceinline__ uint32_t f2tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return r;
+}
+
+// Exchange layout of the received partial scores, chunk-major: 16-byte chunk i (keys
+// 4i..4i+3) of row r at byte (i * 128 + r) * 16, so a warp's 32 rows write and read one
+// contiguous 512-byte span.
+__device__ __forceinline__ uint32_t x_offset(int chunk, int row) { return (chunk * kRows + row) * 16; }
+
+// P layout, UMMA K-major with 128-byte swizzle: key group g (32 keys) is a 16 KB block of
+// 128 rows x 128 bytes; 16-byte chunk c of row r sits at r*128 + (c ^ (r%8))*16.
+__device__ __forceinline__ uint32_t p_offset(int chunk, int row) {
+  return (chunk >> 3) * 16384 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -103,6 +127,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* stages = smem;
   uint8_t* xbuf = smem + kStages * kStageBytes;
   __shared__ Barriers bars;
+  __shared__ float red[kGroups][kRows];  // per-group row maxima, then row sums (epilogue)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -125,16 +150,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int col0 = static_cast<int>(h) * dh;
 
   if (threadIdx.x == 0) {
+    XATTN_TRACE_POINT(14, 0);
     abort_flag = 0;
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
     mbar_init(smem_u32(&bars.s_full), 1);
-    mbar_init(smem_u32(&bars.p_full), kRows);
+    mbar_init(smem_u32(&bars.s_free), kSoftmaxThreads);
+    mbar_init(smem_u32(&bars.p_full), kSoftmaxThreads);
+    for (int b2 = 0; b2 < kXBufs; ++b2) mbar_init(smem_u32(&bars.pv_done[b2]), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
-    mbar_init(smem_u32(&bars.x_full), kRows);
-    mbar_init(smem_u32(&bars.x_empty), kRows);
+    for (int b2 = 0; b2 < kXBufs; ++b2) mbar_init(smem_u32(&bars.x_full[b2]), 1);
+    mbar_init(smem_u32(&bars.x_empty), kSoftmaxThreads / 32);  // one remote arrival per warp
     mbar_init(smem_u32(&bars.drain), 1);
     fence_mbar_init();
   }
@@ -153,16 +181,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
 
+  // Ring order, identical for producer and MMA issuer:
+  //   QK(0), then for j = 0..n-1: [QK(j+1) if any], V(j).
   if (warp == 0) {
     // ================================================================ TMA producer
     if (elect_one() && n_tiles > 0) {
       int s = 0;
       uint32_t phase = 0;
-      for (int j = 0; j < n_tiles && !*abort; ++j) {
+      bool ok = true;
+      auto load_qk = [&](int j) {
         const int key0 = k_begin + j * kKeys;
-        const int valid = min(kKeys, k_end - key0);
-        for (int c = 0; c < n_qk_chunks; ++c) {
-          if (!mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)) break;
+        XATTN_TRACE_POINT(0, j);
+        for (int c = 0; c < n_qk_chunks && ok; ++c) {
+          if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)))
+            break;
           const uint32_t st = smem_u32(stages + s * kStageBytes);
           const uint32_t fb = smem_u32(&bars.full[s]);
           mbar_arrive_expect_tx(fb, kStageBytes);
@@ -170,9 +202,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           tma_load_3d(st + 16384, &p.tk, fb, col0 + c * kChunk, key0, b);
           if (++s == kStages) { s = 0; phase ^= 1u; }
         }
+      };
+      auto load_v = [&](int j) {
+        const int key0 = k_begin + j * kKeys;
+        const int valid = min(kKeys, k_end - key0);
         const int n_v = (valid + kVKeys - 1) / kVKeys;
-        for (int v = 0; v < n_v && !*abort; ++v) {
-          if (!mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)) break;
+        XATTN_TRACE_POINT(1, j);
+        for (int v = 0; v < n_v && ok; ++v) {
+          if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)))
+            break;
           const uint32_t st = smem_u32(stages + s * kStageBytes);
           const uint32_t fb = smem_u32(&bars.full[s]);
           mbar_arrive_expect_tx(fb, n_qk_chunks * kVKeys * 128);
@@ -181,6 +219,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         key0 + v * kVKeys, b);
           if (++s == kStages) { s = 0; phase ^= 1u; }
         }
+      };
+      load_qk(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) load_qk(j + 1);
+        load_v(j);
       }
       // Drain: every load issued must land before this CTA may exit.
       for (int i = 0; i < kStages; ++i) {
@@ -194,44 +237,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (n_tiles > 0) {
         int s = 0;
         uint32_t phase = 0;
+        bool ok = true;
         const uint32_t t_s = tmem + kSCol;
-        for (int j = 0; j < n_tiles; ++j) {
+        auto mma_qk = [&](int j) {
           const int key0 = k_begin + j * kKeys;
           const int valid = min(kKeys, k_end - key0);
           const int n_qk = (valid + 15) & ~15;  // UMMA N: multiple of 16 for M=128
-          const uint32_t idesc_qk = instr_desc(2, kRows, n_qk, false, false);
-          bool ok = true;
-          for (int c = 0; c < n_qk_chunks; ++c) {
+          const uint32_t idesc = instr_desc(2, kRows, n_qk, false, false);
+          for (int c = 0; c < n_qk_chunks && ok; ++c) {
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
+            if (c == 0) XATTN_TRACE_POINT(2, j);
             tc_fence_after();
             const uint32_t st = smem_u32(stages + s * kStageBytes);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = smem_desc(st + kk * 32, 16, 1024, kSw128);
               const uint64_t bd = smem_desc(st + 16384 + kk * 32, 16, 1024, kSw128);
-              mma_tf32_ss(t_s, ad, bd, idesc_qk, (c | kk) != 0);
+              mma_tf32_ss(t_s, ad, bd, idesc, (c | kk) != 0);
             }
             mma_commit(smem_u32(&bars.empty[s]));
             if (++s == kStages) { s = 0; phase ^= 1u; }
           }
-          if (!ok) break;
-          mma_commit(smem_u32(&bars.s_full));
-          if (!mbar_wait(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort)) break;
+          if (ok) mma_commit(smem_u32(&bars.s_full));
+          XATTN_TRACE_POINT(3, j);
+        };
+        mma_qk(0);
+        for (int j = 0; j < n_tiles && ok; ++j) {
+          if (j + 1 < n_tiles) {
+            // S of tile j must have left tensor memory before Q.K^T of tile j+1 lands there.
+            if (!(ok = mbar_wait(smem_u32(&bars.s_free), j & 1, kTimeoutSoftmax, abort))) break;
+            tc_fence_after();
+            mma_qk(j + 1);
+            if (!ok) break;
+          }
+          if (!(ok = mbar_wait(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
+          XATTN_TRACE_POINT(4, j);
           tc_fence_after();
+          const int key0 = k_begin + j * kKeys;
+          const int valid = min(kKeys, k_end - key0);
           const int n_v = (valid + kVKeys - 1) / kVKeys;
+          const uint32_t xb = smem_u32(xbuf + (j & 1) * kXBytes);  // P of tile j
           for (int v = 0; v < n_v; ++v) {
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
             tc_fence_after();
             const uint32_t st = smem_u32(stages + s * kStageBytes);
             const int ksteps = min(2, (valid - v * kVKeys + 7) / 8);
             for (int kk = 0; kk < ksteps; ++kk) {
-              const uint32_t a_tmem = t_s + v * kVKeys + kk * 8;
+              // A = P, keys 16v + 8kk .. +7: key group (16v)/32, byte offset inside the row
+              const int key = v * kVKeys + kk * 8;
+              const uint64_t ad = smem_desc(xb + (key >> 5) * 16384 + (key & 31) * 4, 16, 1024, kSw128);
               // O columns [0, 256) and [256, dh): at most two instructions (N <= 256).
               for (int n0 = 0; n0 < dh; n0 += 256) {
                 const int nn = min(256, dh - n0);
                 const uint64_t bd = smem_desc(st + (n0 / kChunk) * (kVKeys * 128) + kk * 1024,
                                               kVKeys * 128, 512, kSw128Atom32);
-                mma_tf32_ts(tmem + n0, a_tmem, bd, instr_desc(2, kRows, nn, false, true),
+                mma_tf32_ss(tmem + n0, ad, bd, instr_desc(2, kRows, nn, false, true),
                             (j | v | kk) != 0);
               }
             }
@@ -239,6 +299,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (++s == kStages) { s = 0; phase ^= 1u; }
           }
           if (!ok) break;
+          mma_commit(smem_u32(&bars.pv_done[j & 1]));
+          XATTN_TRACE_POINT(5, j);
         }
         mma_commit(smem_u32(&bars.o_done));
       }
@@ -247,59 +309,84 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // ================================================================ softmax / epilogue
+    const int sw = warp - 2;
     const int quad = warp & 3;
+    const int grp = sw >> 2;
     const int row = quad * 32 + lane;
+    const int cbase = grp * kGroupCols;
+    const int ch0 = cbase / 4;  // first 16-byte score chunk of this thread
     const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    const uint32_t x_row = smem_u32(xbuf) + row * (kKeys * 4);
-    const uint32_t peer_x_row = mapa_shared(x_row, peer);
-    const uint32_t peer_x_full = mapa_shared(smem_u32(&bars.x_full), peer);
+    const uint32_t peer_x_row0 = mapa_shared(smem_u32(xbuf) + x_offset(0, row), peer);
+    const uint32_t peer_x_full0 = mapa_shared(smem_u32(&bars.x_full[0]), peer);
     const uint32_t peer_x_empty = mapa_shared(smem_u32(&bars.x_empty), peer);
-    const uint32_t swz = static_cast<uint32_t>(row & 7);
+    const bool arm_thread = (sw == 0 && lane == 0);
 
     float m_run = -INFINITY;   // reference max used for P (log2 units, lazily updated)
     float m_true = -INFINITY;  // exact running max (log2 units)
-    float l_run = 0.f;
+    float l_run = 0.f;         // this group's share of the row sum
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int key0 = k_begin + j * kKeys;
       const int valid = min(kKeys, k_end - key0);
+      // ---- copy S_h out of tensor memory, release the columns to the next Q.K^T
       if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort))) break;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(6, j);
       tc_fence_after();
-      float s[kKeys];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_s_addr(t_row, c), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-      }
-      // ---- exchange partial scores with the peer CTA (other half of D)
-      if (j > 0 && !(ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (j - 1) & 1,
-                                                kTimeoutExchange, abort)))
+      uint32_t ra[32], rb[32];
+      tmem_ld32(t_row + kSCol + cbase, ra);
+      tmem_ld32(t_row + kSCol + cbase + 32, rb);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&bars.s_free));
+      // ---- send S_h into the peer's buffer (j % 2) once the peer has released it
+      const int xb_i = j & 1;
+      uint8_t* xcur = xbuf + xb_i * kXBytes;
+      const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
+      const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
+      if (j >= kXBufs && !(ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), j & 1,
+                                                      kTimeoutExchange, abort)))
         break;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
 #pragma unroll
-      for (int c = 0; c < kKeys / 4; ++c)
-        st_cluster_v4(peer_x_row + ((c ^ swz) << 4), s[4 * c], s[4 * c + 1], s[4 * c + 2],
-                      s[4 * c + 3]);
-      mbar_arrive_remote(peer_x_full);
-      if (!(ok = warp_mbar_wait<true>(smem_u32(&bars.x_full), j & 1, kTimeoutPeer, abort))) break;
+      for (int i = 0; i < 8; ++i)
+        st_async_v4(peer_x_row + (ch0 + i) * (kRows * 16), peer_x_full, __uint_as_float(ra[4 * i]),
+                    __uint_as_float(ra[4 * i + 1]), __uint_as_float(ra[4 * i + 2]),
+                    __uint_as_float(ra[4 * i + 3]));
 #pragma unroll
-      for (int c = 0; c < kKeys / 4; ++c) {
-        const float4 o = *reinterpret_cast<const float4*>(xbuf + row * (kKeys * 4) + ((c ^ swz) << 4));
-        s[4 * c] += o.x;
-        s[4 * c + 1] += o.y;
-        s[4 * c + 2] += o.z;
-        s[4 * c + 3] += o.w;
+      for (int i = 0; i < 8; ++i)
+        st_async_v4(peer_x_row + (ch0 + 8 + i) * (kRows * 16), peer_x_full,
+                    __uint_as_float(rb[4 * i]), __uint_as_float(rb[4 * i + 1]),
+                    __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
+      if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[xb_i]), kXBytes);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
+      if (!(ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), (j >> 1) & 1, kTimeoutPeer,
+                                       abort)))
+        break;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
+      // ---- full score = own + peer, in log2 units, masked; group row max
+      float gmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(ch0 + i, row));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = cbase + 4 * i + e;
+          uint32_t& rv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
+          const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
+          const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
+          gmax = fmaxf(gmax, t);
+          rv = __float_as_uint(t);
+        }
       }
-      mbar_arrive_remote(peer_x_empty);
-      // ---- online softmax, log2 domain
-      float tmax = -INFINITY;
+      red[grp][row] = gmax;
+      // every received score is read before P overwrites the buffer in another layout
+      named_bar_sync(1, kSoftmaxThreads);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(9, j);
+      float tmax = red[0][row];
 #pragma unroll
-      for (int i = 0; i < kKeys; ++i) {
-        s[i] = (i < valid) ? s[i] * p.scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, s[i]);
-      }
+      for (int g = 1; g < kGroups; ++g) tmax = fmaxf(tmax, red[g][row]);
+      // the row maxima are read by both groups before either writes the next tile's
+      named_bar_sync(2 + quad, 32 * kGroups);
       m_true = fmaxf(m_true, tmax);
       float alpha = 1.f;
       if (j == 0) {
@@ -308,41 +395,63 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         alpha = ex2_approx(m_run - tmax);
         m_run = tmax;
       }
-      // O rescale (rare): warp-collective TMEM traffic, only when some row needs it.
+      // O rescale (rare): O must hold every earlier P.V, so wait for the previous one.
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
-        for (int c = 0; c < dh / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
+                                  kTimeoutMmaDone, abort)))
+          break;
+        tc_fence_after();
+        for (int c = grp; c < dh / 32; c += kGroups) {
+          uint32_t o[32];
+          tmem_ld32(t_row + c * 32, o);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(t_row + c * 32, r);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_row + c * 32, o);
         }
+        tmem_st_wait();
       }
       l_run *= alpha;
+      // ---- P = 2^(t - m), rounded to tf32, into the buffer as the A operand of P.V
       float lsum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
+      for (int i = 0; i < 16; ++i) {
+        uint32_t q4[4];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const uint32_t pv = f2tf32(ex2_approx(s[c * 32 + i] - m_run));
-          lsum += __uint_as_float(pv);
-          r[i] = pv;
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t tv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
+          q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
+          lsum += __uint_as_float(q4[e]);
         }
-        tmem_st32(t_s_addr(t_row, c), r);
+        *reinterpret_cast<uint4*>(xcur + p_offset(ch0 + i, row)) =
+            make_uint4(q4[0], q4[1], q4[2], q4[3]);
       }
       l_run += lsum;
-      tmem_st_wait();
+      fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(smem_u32(&bars.p_full));
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
+      // ---- my buffer (j+1) % 2 held P of tile j-1: once that P.V completed, the peer may
+      // send its scores of tile j+1 into it.
+      if (j >= 1 && j + 1 < n_tiles) {
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
+                                  kTimeoutMmaDone, abort)))
+          break;
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
+        if (lane == 0) mbar_arrive_remote(peer_x_empty);
+      }
     }
     // ---- epilogue
+    red[grp][row] = l_run;
+    named_bar_sync(2 + quad, 32 * kGroups);
+    float l_tot = 0.f;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) l_tot += red[g][row];
+    const int grow = row0 + row;
+    const bool live = grow < p.n_latent;
     if (ok && n_tiles > 0 &&
         warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
       tc_fence_after();
-      const int grow = row0 + row;
-      const bool live = grow < p.n_latent;
       float scale;
       float* dst;
       if (p.split_mode) {
@@ -351,42 +460,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         scale = f * p.out_comp;
         const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
         dst = p.po + pidx * p.dim + col0;
-        if (live && h == 0) {
+        if (live && h == 0 && grp == 0) {
           p.pm[pidx] = m_true * 0.69314718055994531f;
-          p.pl[pidx] = l_run * f;
+          p.pl[pidx] = l_tot * f;
         }
       } else {
-        scale = p.out_comp / l_run;
+        scale = p.out_comp / l_tot;
         dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.dim + col0;
       }
-      for (int c = 0; c < dh / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c * 32, r);
+      for (int c = grp; c < dh / 32; c += kGroups) {
+        uint32_t o[32];
+        tmem_ld32(t_row + c * 32, o);
         tmem_ld_wait();
         if (live) {
           float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
 #pragma unroll
           for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(r[4 * i]) * scale, __uint_as_float(r[4 * i + 1]) * scale,
-                                __uint_as_float(r[4 * i + 2]) * scale,
-                                __uint_as_float(r[4 * i + 3]) * scale);
+            d4[i] = make_float4(__uint_as_float(o[4 * i]) * scale, __uint_as_float(o[4 * i + 1]) * scale,
+                                __uint_as_float(o[4 * i + 2]) * scale,
+                                __uint_as_float(o[4 * i + 3]) * scale);
         }
       }
-    } else if (n_tiles == 0 && p.split_mode) {
+    } else if (n_tiles == 0 && p.split_mode && live) {
       // Empty split (upstream kernel_splitk.cu:62-71): m = -FLT_MAX, l = 0, O = 0.
-      const int grow = row0 + row;
-      if (grow < p.n_latent) {
-        const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
-        float* dst = p.po + pidx * p.dim + col0;
-        for (int c = 0; c < dh; ++c) dst[c] = 0.f;
-        if (h == 0) {
-          p.pm[pidx] = -3.4028234663852886e38f;
-          p.pl[pidx] = 0.f;
-        }
+      const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
+      float* dst = p.po + pidx * p.dim + col0;
+      for (int c = grp; c < dh; c += kGroups) dst[c] = 0.f;
+      if (h == 0 && grp == 0) {
+        p.pm[pidx] = -3.4028234663852886e38f;
+        p.pl[pidx] = 0.f;
       }
     }
   }
 
+  if (threadIdx.x == 0) XATTN_TRACE_POINT(13, 0);
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // the peer may still be writing into this CTA's exchange buffer

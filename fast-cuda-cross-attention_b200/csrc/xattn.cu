@@ -517,3 +517,10 @@ extern "C" int xattn_selftest_timeout(int bound_us) {
 }
 
 extern "C" int xattn_version(void) { return kVersion; }
+
+#ifdef XATTN_TRACE
+// Development builds only: copies the device timeline buffer to `host` (16*16*16 u64).
+extern "C" int xattn_trace_fetch(unsigned long long* host) {
+  return static_cast<int>(cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace)));
+}
+#endif
