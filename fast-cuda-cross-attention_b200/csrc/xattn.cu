@@ -524,3 +524,67 @@ extern "C" int xattn_trace_fetch(unsigned long long* host) {
   return static_cast<int>(cudaMemcpyFromSymbol(host, g_trace, sizeof(g_trace)));
 }
 #endif
+
+// ===================================================================== no-allocation split-K
+// xattn_splitk_noalloc: the launch_splitk_kernel computation with its partials in a fixed
+// scratch array that is part of the library image, for callers that may not allocate
+// device memory during a call (see include/xattn.h).  The host never dereferences the
+// array's symbol: it asks the runtime for the array's device address once per device.
+namespace xattn {
+namespace {
+
+constexpr size_t kNoAllocScratchFloats = static_cast<size_t>(8) << 20;  // 32 MiB of fp32
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array on device `dev` (current), looked up on first use.
+float* noalloc_scratch(int dev) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+      return nullptr;
+    g_noalloc_ptr[dev] = static_cast<float*>(ptr);
+  }
+  return g_noalloc_ptr[dev];
+}
+
+size_t round_up64(size_t n) { return (n + 63) / 64 * 64; }  // 256-byte sub-array alignment
+
+}  // namespace
+}  // namespace xattn
+
+extern "C" int xattn_splitk_noalloc(const float* Q, const float* K, const float* V, float* output,
+                                    int batch_size, int N_latent, int N_input, int dim,
+                                    int num_splits, cudaStream_t stream) {
+  if (bad_sizes(batch_size, N_latent, N_input, dim) || num_splits <= 0)
+    return set_error(XATTN_ERR_ARG);
+  if (batch_size == 0 || N_latent == 0) return set_error(XATTN_OK);
+  if (output == nullptr) return set_error(XATTN_ERR_ARG);
+  if (N_input == 0) return set_error(zero_output(output, batch_size, N_latent, dim, stream));
+  if (Q == nullptr || K == nullptr || V == nullptr) return set_error(XATTN_ERR_ARG);
+  const size_t rows = static_cast<size_t>(batch_size) * N_latent;
+  const size_t po_elems = round_up64(rows * num_splits * dim);
+  const size_t ml_elems = round_up64(rows * num_splits);
+  if (po_elems + 2 * ml_elems > kNoAllocScratchFloats) return set_error(XATTN_ERR_TOO_LARGE);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return set_error(rc);
+  float* po = noalloc_scratch(dev);
+  if (po == nullptr) return set_error(XATTN_ERR_LAUNCH);
+  float* pm = po + po_elems;
+  float* pl = pm + ml_elems;
+  const int chunk = std::max(1, (N_input + num_splits - 1) / num_splits);  // kernel_splitk.cu:59
+  const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(dim));
+  if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, output, dim))
+    rc = launch_simt<float, float>(Q, K, V, nullptr, po, pm, pl, batch_size, 1, N_latent, N_input,
+                                   dim, num_splits, chunk, 1, scale_log2, stream);
+  else
+    rc = launch_fused(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim,
+                      num_splits, chunk, 1, stream);
+  if (rc != XATTN_OK) return set_error(rc);
+  return set_error(launch_combine(po, pm, pl, output, static_cast<long long>(rows), dim,
+                                  num_splits, stream));
+}

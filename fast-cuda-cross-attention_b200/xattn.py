@@ -43,7 +43,7 @@ EXPORTED = (
     "launch_wmma_splitk_kernel", "xattn_fp32", "xattn_fp32_partial", "xattn_combine",
     "xattn_lse_pack", "xattn_lse_rescale", "xattn_lse_finalize", "xattn_bf16_mha",
     "xattn_last_error", "xattn_status", "xattn_set_option", "xattn_selftest_timeout",
-    "xattn_version", "xattn_plan_fp32",
+    "xattn_version", "xattn_plan_fp32", "xattn_splitk_noalloc",
 )
 
 OPT_PATH, OPT_SPLITS, OPT_WAIT_US, OPT_TF32_COMP = 1, 2, 3, 4
@@ -79,6 +79,7 @@ def lib():
         "xattn_selftest_timeout": ([i], i),
         "xattn_version": ([], i),
         "xattn_plan_fp32": ([i, i, i, i, ctypes.POINTER(i)], i),
+        "xattn_splitk_noalloc": ([vp] * 4 + [i] * 5 + [vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)

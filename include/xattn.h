@@ -88,6 +88,7 @@ void launch_wmma_splitk_kernel(const __half* Q, const __half* K, const __half* V
 #define XATTN_ERR_LAUNCH 2     /* a kernel launch failed (see cudaGetLastError)         */
 #define XATTN_ERR_NOMEM 3      /* the library workspace could not be grown              */
 #define XATTN_ERR_DEVICE 4     /* a device wait timed out (see xattn_status)            */
+#define XATTN_ERR_TOO_LARGE 5  /* the problem needs more scratch than the fixed array    */
 
 /* Status-returning form of launch_optimized_kernel (no counterpart upstream).          */
 int xattn_fp32(const float* Q, const float* K, const float* V, float* output, int batch_size,
@@ -129,6 +130,30 @@ int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bf
  * pointers: returns the number of kernels the call launches (1, or 2 with a key split
  * and its merge) and stores the key-split count in *num_splits (may be NULL).          */
 int xattn_plan_fp32(int batch_size, int N_latent, int N_input, int dim, int* num_splits);
+
+/* Split-K attention that allocates nothing.  No counterpart in the upstream project.
+ *
+ * Same key-split rule, result and tolerance as launch_splitk_kernel, but the caller passes
+ * only Q, K, V and the output: the (m, l, O) partials live in one scratch array compiled
+ * into the library (32 MiB, held by every GPU that loads the library until the process
+ * exits).  It is meant for callers that may not allocate device memory during a call:
+ * programs that hand the whole GPU to their own memory pool at start-up, where an extra
+ * cudaMalloc would fail or fragment that pool, and latency-critical loops that cannot
+ * afford the device-wide synchronisation a cudaMalloc / cudaFree can cause.  (The
+ * automatic split of launch_optimized_kernel grows a library workspace with cudaMalloc;
+ * launch_splitk_kernel needs caller-allocated scratch.)
+ *
+ * Limit: batch_size * N_latent * num_splits * (dim + 2) floats <= 8,388,608 (32 MiB);
+ * larger problems return XATTN_ERR_TOO_LARGE without launching anything.  The first call
+ * on a device looks up the array's device address (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  Every call on a device uses
+ * the same array and leaves the last call's partials in it; nothing in it has to start at
+ * zero (every partial a call reads, that call writes first).  Calls whose kernels overlap
+ * on the GPU (different streams, or different host threads without ordering) race on the
+ * array: order them on one stream.                                                      */
+int xattn_splitk_noalloc(const float* Q, const float* K, const float* V, float* output,
+                         int batch_size, int N_latent, int N_input, int dim, int num_splits,
+                         cudaStream_t stream);
 
 /* Host-side status of the most recent call on this thread (XATTN_* code).              */
 int xattn_last_error(void);
