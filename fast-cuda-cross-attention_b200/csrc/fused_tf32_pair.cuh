@@ -1,0 +1,478 @@
+// Fused fp32-API cross attention on 4-CTA clusters: a cta_group::2 row pair per D half.
+//
+// Same computation and epilogue as fused_tf32.cuh (read that file first); this variant
+// changes how one SM's share of the work is fed.  A cluster of four CTAs owns 256 query rows
+// of one batch:  rank = 2h + r, where h is the half of D the CTA owns (as in the two-CTA
+// kernel) and r the 128-row half.  The two CTAs with the same h form a cta_group::2 pair:
+// the pair leader (r = 0) issues every MMA for both, with M = 256 rows; the K operand of
+// Q.K^T and the V operand of P.V are split between the pair's shared memories (each CTA
+// loads half the keys of K and half the columns of V), so every K/V byte is loaded once per
+// 256 queries instead of once per 128.  Per key tile and CTA that is 384 KB of operands
+// (Q 192 + K 96 + V 96) instead of 576 KB, and half the shared-memory reads of K and V.
+// Scores are still exchanged between the two D halves (ranks r and r + 2) through
+// distributed shared memory; P stays per CTA (each CTA supplies its own 128 rows of P as
+// the A operand of the pair MMA).
+//
+// Pair protocol.  TMA loads of both CTAs complete on the leader's full barrier; the
+// leader's commits are multicast to both CTAs (empty, s_full, pv_done, o_done); the
+// softmax warps of both CTAs release S and publish P by one arrival per warp on the
+// leader's s_free / p_full barriers.  No TMA multicast is used.
+#pragma once
+
+#include "fused_tf32.cuh"
+
+namespace xattn {
+namespace pair4 {
+
+using fused::f2tf32;
+using fused::kChunk;
+using fused::kGroupCols;
+using fused::kGroups;
+using fused::kKeys;
+using fused::kRescaleLog2;
+using fused::kRows;
+using fused::kSCol;
+using fused::kSoftmaxThreads;
+using fused::kTmemCols;
+using fused::kXBytes;
+using fused::p_offset;
+using fused::Params;
+using fused::x_offset;
+
+constexpr int kVKeys = 32;           // keys per V chunk (four K=8 steps)
+constexpr int kStageBytes = 24576;   // Q chunk 16 KB + K half 8 KB, or a V chunk
+// Exchange / P buffers: 1 (deep ring: 6 stages, 144 KB of operands in flight) or 2 (the
+// next tile's exchange overlaps this tile's P.V; 4 stages).
+constexpr int kXBufs = 2;
+constexpr int kStages = kXBufs == 1 ? 6 : 4;
+constexpr int kThreads = 64 + kSoftmaxThreads;
+constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
+constexpr int kStaticSmemBytes = 1536;
+static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
+constexpr int kSoftmaxWarpsPerPair = 2 * kSoftmaxThreads / 32;
+
+// D halves this kernel takes: one pair instruction covers N = dh (dh <= 256) or two of
+// N = dh / 2 (dh = 384); each CTA holds N / 2 columns of V per instruction, whole 32-wide
+// slabs.
+__host__ __device__ constexpr bool supports_dh(int dh) {
+  return dh == 64 || dh == 128 || dh == 192 || dh == 256 || dh == 384;
+}
+
+struct __align__(8) Barriers {
+  uint64_t full[kStages];   // leader: both CTAs' loads of a stage landed
+  uint64_t empty[kStages];  // both: the pair MMA consumed a stage (multicast commit)
+  uint64_t s_full;          // both: S tile ready (multicast)
+  uint64_t s_free;          // leader: both CTAs copied S out of TMEM
+  uint64_t p_full;          // leader: both CTAs wrote P
+  uint64_t pv_done[kXBufs]; // both: P.V on buffer b complete (multicast)
+  uint64_t o_done;          // both: last P.V complete (multicast)
+  uint64_t x_full[kXBufs];  // D-peer -> me: partial scores in my buffer b
+  uint64_t x_empty;         // D-peer -> me: its buffer for my next send may be refilled
+  uint64_t drain;           // leader: its MMAs completed
+};
+
+__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
+    fused_tf32_pair_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* stages = smem;
+  uint8_t* xbuf = smem + kStages * kStageBytes;
+  __shared__ Barriers bars;
+  __shared__ float red[kGroups][kRows];
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const uint32_t r = rank & 1u;           // row half (position in the cta_group::2 pair)
+  const uint32_t h = rank >> 1;           // D half
+  const uint32_t leader = rank & ~1u;     // pair leader
+  const uint32_t dpeer = rank ^ 2u;       // same rows, other D half
+  const uint16_t pair_mask = static_cast<uint16_t>(3u << leader);
+  const bool is_leader = (r == 0);
+
+  // ---- work item: (batch, 256-row block, split)
+  const int item = blockIdx.x / 4;
+  const int n_rb2 = (p.n_latent + 2 * kRows - 1) / (2 * kRows);
+  const int split = item % p.num_splits;
+  const int rb2 = (item / p.num_splits) % n_rb2;
+  const int b = item / (p.num_splits * n_rb2);
+  const int row0 = rb2 * 2 * kRows + static_cast<int>(r) * kRows;  // this CTA's rows
+  const int k_begin = split * p.split_chunk;
+  const int k_end = min(k_begin + p.split_chunk, p.n_input);
+  const int n_tiles = k_end > k_begin ? (k_end - k_begin + kKeys - 1) / kKeys : 0;
+  const int dh = p.dh;
+  const int n_qk_chunks = dh / kChunk;
+  const int col0 = static_cast<int>(h) * dh;
+  const int n_instr = dh <= 256 ? 1 : 2;         // P.V instructions per K step
+  const int nn = dh / n_instr;                    // pair N per instruction
+  const int spi = nn / 64;                        // 32-wide V slabs per CTA per instruction
+  const int n_slabs = spi * n_instr;              // V slabs this CTA loads per chunk
+
+  if (threadIdx.x == 0) {
+    XATTN_TRACE_POINT(14, 0);
+    abort_flag = 0;
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bars.s_full), 1);
+    mbar_init(smem_u32(&bars.s_free), kSoftmaxWarpsPerPair);
+    mbar_init(smem_u32(&bars.p_full), kSoftmaxWarpsPerPair);
+    for (int i = 0; i < kXBufs; ++i) {
+      mbar_init(smem_u32(&bars.pv_done[i]), 1);
+      mbar_init(smem_u32(&bars.x_full[i]), 1);
+    }
+    mbar_init(smem_u32(&bars.o_done), 1);
+    mbar_init(smem_u32(&bars.x_empty), kSoftmaxThreads / 32);
+    mbar_init(smem_u32(&bars.drain), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc_pair(smem_u32(&tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  if (warp == 1 && lane == 0) {
+    tma_prefetch_desc(&p.tq);
+    tma_prefetch_desc(&p.tk);
+    tma_prefetch_desc(&p.tv);
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 0) {
+    // ================================================================ TMA producer (both CTAs)
+    if (elect_one() && n_tiles > 0) {
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      auto stage_begin = [&](uint32_t bytes_per_cta) -> uint32_t {
+        if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)))
+          return 0;
+        if (is_leader) mbar_arrive_expect_tx(smem_u32(&bars.full[s]), 2 * bytes_per_cta);
+        return mapa_shared(smem_u32(&bars.full[s]), leader);
+      };
+      auto stage_end = [&]() {
+        if (++s == kStages) { s = 0; phase ^= 1u; }
+      };
+      auto load_qk = [&](int j) {
+        const int key0 = k_begin + j * kKeys;
+        const int valid = min(kKeys, k_end - key0);
+        const int n_qk = (valid + 15) & ~15;
+        const int kbase = key0 + static_cast<int>(r) * (n_qk / 2);  // this CTA's half of the keys
+        XATTN_TRACE_POINT(0, j);
+        for (int c = 0; c < n_qk_chunks && ok; ++c) {
+          const uint32_t fb = stage_begin(16384 + 8192);
+          if (!ok) break;
+          const uint32_t st = smem_u32(stages + s * kStageBytes);
+          tma_load_3d_pair(st, &p.tq, fb, col0 + c * kChunk, row0, b);
+          tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * kChunk, kbase, b);
+          stage_end();
+        }
+      };
+      auto load_v = [&](int j) {
+        const int key0 = k_begin + j * kKeys;
+        const int valid = min(kKeys, k_end - key0);
+        const int n_v = (valid + kVKeys - 1) / kVKeys;
+        XATTN_TRACE_POINT(1, j);
+        for (int v = 0; v < n_v && ok; ++v) {
+          const uint32_t fb = stage_begin(n_slabs * kVKeys * 128);
+          if (!ok) break;
+          const uint32_t st = smem_u32(stages + s * kStageBytes);
+          for (int i = 0; i < n_slabs; ++i) {
+            const int n = i / spi, jj = i % spi;
+            const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2) + jj * kChunk;
+            tma_load_3d_pair(st + i * (kVKeys * 128), &p.tv, fb, dim, key0 + v * kVKeys, b);
+          }
+          stage_end();
+        }
+      };
+      load_qk(0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) load_qk(j + 1);
+        load_v(j);
+      }
+      // Drain: the pair MMA releases every stage it consumed; wait for the last ones so no
+      // load into this CTA's shared memory is still in flight at exit.
+      for (int i = 0; i < kStages; ++i) {
+        if (--s < 0) { s = kStages - 1; phase ^= 1u; }
+        mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer (pair leader)
+    if (is_leader && elect_one()) {
+      if (n_tiles > 0) {
+        int s = 0;
+        uint32_t phase = 0;
+        bool ok = true;
+        const uint32_t t_s = tmem + kSCol;
+        auto mma_qk = [&](int j) {
+          const int key0 = k_begin + j * kKeys;
+          const int valid = min(kKeys, k_end - key0);
+          const int n_qk = (valid + 15) & ~15;
+          const uint32_t idesc = instr_desc(2, 2 * kRows, n_qk, false, false);
+          for (int c = 0; c < n_qk_chunks && ok; ++c) {
+            if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
+            if (c == 0) XATTN_TRACE_POINT(2, j);
+            tc_fence_after();
+            const uint32_t st = smem_u32(stages + s * kStageBytes);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = smem_desc(st + kk * 32, 16, 1024, kSw128);
+              const uint64_t bd = smem_desc(st + 16384 + kk * 32, 16, 1024, kSw128);
+              mma_tf32_ss_pair(t_s, ad, bd, idesc, (c | kk) != 0);
+            }
+            mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
+            if (++s == kStages) { s = 0; phase ^= 1u; }
+          }
+          if (ok) mma_commit_pair_mc(smem_u32(&bars.s_full), pair_mask);
+          XATTN_TRACE_POINT(3, j);
+        };
+        mma_qk(0);
+        for (int j = 0; j < n_tiles && ok; ++j) {
+          if (j + 1 < n_tiles) {
+            if (!(ok = mbar_wait<true>(smem_u32(&bars.s_free), j & 1, kTimeoutSoftmax, abort))) break;
+            tc_fence_after();
+            mma_qk(j + 1);
+            if (!ok) break;
+          }
+          if (!(ok = mbar_wait<true>(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
+          XATTN_TRACE_POINT(4, j);
+          tc_fence_after();
+          const int key0 = k_begin + j * kKeys;
+          const int valid = min(kKeys, k_end - key0);
+          const int n_v = (valid + kVKeys - 1) / kVKeys;
+          const uint32_t xb = smem_u32(xbuf + (j % kXBufs) * kXBytes);
+          const uint32_t idesc_pv = instr_desc(2, 2 * kRows, nn, false, true);
+          for (int v = 0; v < n_v; ++v) {
+            if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
+            tc_fence_after();
+            const uint32_t st = smem_u32(stages + s * kStageBytes);
+            const int ksteps = min(kVKeys / 8, (valid - v * kVKeys + 7) / 8);
+            for (int kk = 0; kk < ksteps; ++kk) {
+              const int key = v * kVKeys + kk * 8;
+              const uint64_t ad = smem_desc(xb + (key >> 5) * 16384 + (key & 31) * 4, 16, 1024, kSw128);
+              for (int n = 0; n < n_instr; ++n) {
+                const uint64_t bd = smem_desc(st + n * spi * (kVKeys * 128) + kk * 1024,
+                                              kVKeys * 128, 512, kSw128Atom32);
+                mma_tf32_ss_pair(tmem + n * nn, ad, bd, idesc_pv, (j | v | kk) != 0);
+              }
+            }
+            mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
+            if (++s == kStages) { s = 0; phase ^= 1u; }
+          }
+          if (!ok) break;
+          mma_commit_pair_mc(smem_u32(&bars.pv_done[j % kXBufs]), pair_mask);
+          XATTN_TRACE_POINT(5, j);
+        }
+        mma_commit_pair_mc(smem_u32(&bars.o_done), pair_mask);
+      }
+      mma_commit_pair_mc(smem_u32(&bars.drain), static_cast<uint16_t>(1u << rank));
+      mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, nullptr);
+    }
+  } else {
+    // ================================================================ softmax / epilogue (both)
+    const int sw = warp - 2;
+    const int quad = warp & 3;
+    const int grp = sw >> 2;
+    const int row = quad * 32 + lane;
+    const int cbase = grp * kGroupCols;
+    const int ch0 = cbase / 4;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t peer_x_row0 = mapa_shared(smem_u32(xbuf) + x_offset(0, row), dpeer);
+    const uint32_t peer_x_full0 = mapa_shared(smem_u32(&bars.x_full[0]), dpeer);
+    const uint32_t peer_x_empty = mapa_shared(smem_u32(&bars.x_empty), dpeer);
+    const uint32_t lead_s_free = mapa_shared(smem_u32(&bars.s_free), leader);
+    const uint32_t lead_p_full = mapa_shared(smem_u32(&bars.p_full), leader);
+    const bool arm_thread = (sw == 0 && lane == 0);
+
+    float m_run = -INFINITY;
+    float m_true = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int key0 = k_begin + j * kKeys;
+      const int valid = min(kKeys, k_end - key0);
+      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort))) break;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(6, j);
+      tc_fence_after();
+      uint32_t ra[32], rb[32];
+      tmem_ld32(t_row + kSCol + cbase, ra);
+      tmem_ld32(t_row + kSCol + cbase + 32, rb);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(lead_s_free);
+      // buffer of tile j: j % kXBufs, used for the (j / kXBufs)-th time
+      const int xb_i = j % kXBufs;
+      const uint32_t xb_par = static_cast<uint32_t>(j / kXBufs) & 1u;
+      if (kXBufs == 1 && j >= 1) {
+        // single buffer: it held P of tile j-1; free once that P.V completed
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[0]), (j - 1) & 1, kTimeoutMmaDone, abort)))
+          break;
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
+        if (lane == 0) mbar_arrive_remote(peer_x_empty);
+      }
+      uint8_t* xcur = xbuf + xb_i * kXBytes;
+      const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
+      const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
+      if (j >= kXBufs && !(ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (j - kXBufs) & 1,
+                                                      kTimeoutExchange, abort)))
+        break;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        st_async_v4(peer_x_row + (ch0 + i) * (kRows * 16), peer_x_full, __uint_as_float(ra[4 * i]),
+                    __uint_as_float(ra[4 * i + 1]), __uint_as_float(ra[4 * i + 2]),
+                    __uint_as_float(ra[4 * i + 3]));
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        st_async_v4(peer_x_row + (ch0 + 8 + i) * (kRows * 16), peer_x_full,
+                    __uint_as_float(rb[4 * i]), __uint_as_float(rb[4 * i + 1]),
+                    __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
+      if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[xb_i]), kXBytes);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
+      if (!(ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), xb_par, kTimeoutPeer, abort)))
+        break;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
+      float gmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(ch0 + i, row));
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = cbase + 4 * i + e;
+          uint32_t& rv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
+          const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
+          const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
+          gmax = fmaxf(gmax, t);
+          rv = __float_as_uint(t);
+        }
+      }
+      red[grp][row] = gmax;
+      named_bar_sync(1, kSoftmaxThreads);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(9, j);
+      float tmax = red[0][row];
+#pragma unroll
+      for (int g = 1; g < kGroups; ++g) tmax = fmaxf(tmax, red[g][row]);
+      named_bar_sync(2 + quad, 32 * kGroups);
+      m_true = fmaxf(m_true, tmax);
+      float alpha = 1.f;
+      if (j == 0) {
+        m_run = tmax;
+      } else if (tmax > m_run + kRescaleLog2) {
+        alpha = ex2_approx(m_run - tmax);
+        m_run = tmax;
+      }
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) % kXBufs]),
+                                  static_cast<uint32_t>((j - 1) / kXBufs) & 1u, kTimeoutMmaDone,
+                                  abort)))
+          break;
+        tc_fence_after();
+        for (int c = grp; c < dh / 32; c += kGroups) {
+          uint32_t o[32];
+          tmem_ld32(t_row + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_row + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      l_run *= alpha;
+      float lsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        uint32_t q4[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const uint32_t tv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
+          q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
+          lsum += __uint_as_float(q4[e]);
+        }
+        *reinterpret_cast<uint4*>(xcur + p_offset(ch0 + i, row)) =
+            make_uint4(q4[0], q4[1], q4[2], q4[3]);
+      }
+      l_run += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(lead_p_full);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
+      if (kXBufs == 2 && j >= 1 && j + 1 < n_tiles) {
+        // double buffer: buffer (j+1) % 2 held P of tile j-1; free once that P.V completed
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j + 1) % kXBufs]),
+                                  static_cast<uint32_t>((j - 1) / kXBufs) & 1u, kTimeoutMmaDone,
+                                  abort)))
+          break;
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
+        if (lane == 0) mbar_arrive_remote(peer_x_empty);
+      }
+    }
+    // ---- epilogue
+    red[grp][row] = l_run;
+    named_bar_sync(2 + quad, 32 * kGroups);
+    float l_tot = 0.f;
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) l_tot += red[g][row];
+    const int grow = row0 + row;
+    const bool live = grow < p.n_latent;
+    if (ok && n_tiles > 0 &&
+        warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
+      tc_fence_after();
+      float scale;
+      float* dst;
+      if (p.split_mode) {
+        const float f = ex2_approx(m_run - m_true);
+        scale = f * p.out_comp;
+        const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
+        dst = p.po + pidx * p.dim + col0;
+        if (live && h == 0 && grp == 0) {
+          p.pm[pidx] = m_true * 0.69314718055994531f;
+          p.pl[pidx] = l_tot * f;
+        }
+      } else {
+        scale = p.out_comp / l_tot;
+        dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.dim + col0;
+      }
+      for (int c = grp; c < dh / 32; c += kGroups) {
+        uint32_t o[32];
+        tmem_ld32(t_row + c * 32, o);
+        tmem_ld_wait();
+        if (live) {
+          float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            d4[i] = make_float4(__uint_as_float(o[4 * i]) * scale, __uint_as_float(o[4 * i + 1]) * scale,
+                                __uint_as_float(o[4 * i + 2]) * scale,
+                                __uint_as_float(o[4 * i + 3]) * scale);
+        }
+      }
+    } else if (n_tiles == 0 && p.split_mode && live) {
+      const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
+      float* dst = p.po + pidx * p.dim + col0;
+      for (int c = grp; c < dh; c += kGroups) dst[c] = 0.f;
+      if (h == 0 && grp == 0) {
+        p.pm[pidx] = -3.4028234663852886e38f;
+        p.pl[pidx] = 0.f;
+      }
+    }
+  }
+
+  if (threadIdx.x == 0) XATTN_TRACE_POINT(13, 0);
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc_pair(tmem, kTmemCols);
+}
+
+}  // namespace pair4
+}  // namespace xattn

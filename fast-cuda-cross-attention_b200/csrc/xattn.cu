@@ -20,6 +20,7 @@
 #include <utility>
 
 #include "fused_tf32.cuh"
+#include "fused_tf32_pair.cuh"
 #include "simt.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -39,6 +40,7 @@ std::atomic<int> g_opt_path{0};
 std::atomic<int> g_opt_splits{0};
 std::atomic<int> g_opt_wait_us{2000000};
 std::atomic<int> g_opt_tf32_comp{1};
+std::atomic<int> g_opt_kernel{0};  // 0 auto, 1 two-CTA kernel, 2 four-CTA pair kernel
 
 int set_error(int code) {
   t_last_error = code;
@@ -65,6 +67,10 @@ int prepare_device(int* dev_out) {
     cudaDeviceGetAttribute(&st.sms, cudaDevAttrMultiProcessorCount, dev);
     if (cudaFuncSetAttribute(fused::fused_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fused::kSmemBytes) != cudaSuccess)
+      return XATTN_ERR_LAUNCH;
+    if (cudaFuncSetAttribute(pair4::fused_tf32_pair_kernel,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             pair4::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
     st.init = true;
   }
@@ -115,14 +121,15 @@ bool tc_fp32_supported(const float* Q, const float* K, const float* V, const flo
 }
 
 bool make_fp32_maps(fused::Params& p, const float* Q, const float* K, const float* V, int B,
-                    int Nl, int Ni, int D) {
+                    int Nl, int Ni, int D, uint32_t k_box = fused::kKeys,
+                    uint32_t v_box = fused::kVKeys) {
   const uint64_t dq[3] = {(uint64_t)D, (uint64_t)Nl, (uint64_t)B};
   const uint64_t sq[2] = {(uint64_t)D * 4, (uint64_t)Nl * D * 4};
   const uint64_t dk[3] = {(uint64_t)D, (uint64_t)Ni, (uint64_t)B};
   const uint64_t sk[2] = {(uint64_t)D * 4, (uint64_t)Ni * D * 4};
   const uint32_t bq[3] = {fused::kChunk, fused::kRows, 1};
-  const uint32_t bk[3] = {fused::kChunk, fused::kKeys, 1};
-  const uint32_t bv[3] = {fused::kChunk, fused::kVKeys, 1};
+  const uint32_t bk[3] = {fused::kChunk, k_box, 1};
+  const uint32_t bv[3] = {fused::kChunk, v_box, 1};
   return encode_tmap(&p.tq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, Q, dq, sq, bq,
                      CU_TENSOR_MAP_SWIZZLE_128B) &&
          encode_tmap(&p.tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, K, dk, sk, bk,
@@ -159,6 +166,44 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
   fused::fused_tf32_kernel<<<static_cast<unsigned>(items * 2), fused::kThreads, fused::kSmemBytes,
                              stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+// Four-CTA pair kernel, normalised output (fused_tf32_pair.cuh).
+int launch_fused_pair(const float* Q, const float* K, const float* V, float* out, int B, int Nl,
+                      int Ni, int D, cudaStream_t stream) {
+  fused::Params p;
+  if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D, fused::kKeys / 2, pair4::kVKeys))
+    return XATTN_ERR_ARG;
+  p.out = out;
+  p.po = p.pm = p.pl = nullptr;
+  p.batch = B;
+  p.n_latent = Nl;
+  p.n_input = Ni;
+  p.dim = D;
+  p.dh = D / 2;
+  p.n_row_blocks = (Nl + 2 * fused::kRows - 1) / (2 * fused::kRows);
+  p.num_splits = 1;
+  p.split_chunk = Ni;
+  p.split_mode = 0;
+  const bool comp = g_opt_tf32_comp.load() != 0;
+  p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(D)) *
+                                    (comp ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
+  p.out_comp = comp ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+  const long long items = static_cast<long long>(B) * p.n_row_blocks;
+  if (items * 4 > 0x7fffffffLL) return XATTN_ERR_ARG;
+  pair4::fused_tf32_pair_kernel<<<static_cast<unsigned>(items * 4), pair4::kThreads,
+                                  pair4::kSmemBytes, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+// The pair kernel pays off once 256-row blocks fill the four-CTA cluster slots
+// (about SMs / 4.5: 33 on a B200 at this shared-memory size).
+bool use_pair_kernel(int dev, int B, int Nl, int D) {
+  const int sel = g_opt_kernel.load();
+  if (sel == 1 || !pair4::supports_dh(D / 2)) return false;
+  if (sel == 2) return true;
+  const long long items = static_cast<long long>(B) * ((Nl + 255) / 256);
+  return items >= sm_count(dev) * 2 / 9;
 }
 
 // ------------------------------------------------------------------ generic path
@@ -256,6 +301,8 @@ int run_fp32(const float* Q, const float* K, const float* V, float* O, int B, in
     return set_error(launch_simt<float, float>(Q, K, V, O, nullptr, nullptr, nullptr, B, 1, Nl, Ni,
                                                D, 1, Ni, 0, scale_log2, stream));
   }
+  if (g_opt_splits.load() <= 0 && use_pair_kernel(dev, B, Nl, D))
+    return set_error(launch_fused_pair(Q, K, V, O, B, Nl, Ni, D, stream));
   int splits = 1, chunk = Ni;
   plan_splits(dev, B, Nl, Ni, path, &splits, &chunk);
   if (splits == 1)
@@ -476,6 +523,7 @@ extern "C" int xattn_set_option(int key, int value) {
     case 2: return g_opt_splits.exchange(value);
     case 3: return g_opt_wait_us.exchange(value > 0 ? value : 2000000);
     case 4: return g_opt_tf32_comp.exchange(value);
+    case 5: return g_opt_kernel.exchange(value);
     default: return -1;
   }
 }

@@ -168,7 +168,9 @@ int xattn_status(int clear);
  * microseconds (default 2,000,000).  key 4 = TF32 truncation-bias compensation of the
  * tensor-core fp32 path: 1 (default) scales scores by (1 + 2e) and the output by (1 + e),
  * e = 2^-11 / (2 ln 2), the mean relative truncation error of one operand; 0 turns it
- * off (for inputs already exact in TF32).  Returns the previous value.                 */
+ * off (for inputs already exact in TF32).  key 5 = fp32 tensor-core kernel: 0 auto, 1 the
+ * two-CTA kernel, 2 the four-CTA pair kernel (where the shape allows it).  Returns the
+ * previous value.                                                                       */
 int xattn_set_option(int key, int value);
 
 /* Runs a kernel that waits on an mbarrier nothing will ever arrive on, with the wait

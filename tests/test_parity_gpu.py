@@ -145,6 +145,46 @@ def test_fp32_shapes_with_guards(X, torch_cuda, shape):
     assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, str(shape))
 
 
+PAIR_SHAPES = [
+    (2, 256, 784, 768), (1, 200, 300, 768), (3, 129, 129, 512), (2, 300, 1000, 256),
+    (1, 64, 100, 128), (4, 512, 784, 384), (1, 1, 1, 768),
+]
+
+
+@pytest.mark.parametrize("shape", PAIR_SHAPES, ids=lambda s: "B%d_Nl%d_Ni%d_D%d" % s)
+def test_four_cta_pair_kernel_shapes(X, torch_cuda, shape):
+    """The cta_group::2 four-CTA kernel, forced on shapes it would not pick by itself."""
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    gen = torch.Generator(device="cuda").manual_seed(7 + sum(shape))
+    q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+    out, intact = guarded_empty(torch, (b, nl, d), torch.float32)
+    prev = X.set_option(X.OPT_KERNEL, 2)
+    try:
+        X.cross_attention(q, k, v, out=out)
+        torch.cuda.synchronize()
+    finally:
+        X.set_option(X.OPT_KERNEL, prev)
+    assert intact(), "write outside the output tensor"
+    assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, "pair " + str(shape))
+
+
+def test_two_and_four_cta_kernels_agree(X, torch_cuda):
+    torch = torch_cuda
+    q, k, v = (torch.randn(8, n, 768, device="cuda") for n in (512, 784, 784))
+    outs = []
+    for sel in (1, 2):
+        prev = X.set_option(X.OPT_KERNEL, sel)
+        try:
+            outs.append(X.cross_attention(q, k, v))
+            torch.cuda.synchronize()
+        finally:
+            X.set_option(X.OPT_KERNEL, prev)
+    ref = ref_attention(torch, q, k, v)
+    for o in outs:
+        assert_close(torch, o, ref, TF32_TOL, "kernel")
+
+
 def test_all_upstream_fp32_names_agree(X, torch_cuda):
     torch = torch_cuda
     L = X.lib()
