@@ -45,7 +45,15 @@ constexpr int kStageBytes = 24576;   // Q chunk 16 KB + K half 8 KB, or a V chun
 // next tile's exchange overlaps this tile's P.V; 4 stages).
 constexpr int kXBufs = 2;
 constexpr int kStages = kXBufs == 1 ? 6 : 4;
-constexpr int kThreads = 64 + kSoftmaxThreads;
+// Warps: 0 producer, 1 MMA issuer, 2..9 softmax, 10.. further producers.  Registers are
+// allocated per group of four warps, so twelve warps cost the softmax warps nothing.
+constexpr int kFirstExtraProducer = 2 + kSoftmaxThreads / 32;
+constexpr int kProducers = 3;
+constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (kProducers - 1);
+// A producer waits for the release of stage i - kStages by parity alone.  That parity cannot
+// alias an older phase because the producer's previous stage, i + kStages - kProducers,
+// already required stage i - kProducers <= i - kStages to be consumed.
+static_assert(kProducers <= kStages, "parity-only empty waits need kProducers <= kStages");
 constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
 constexpr int kStaticSmemBytes = 1536;
 static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
@@ -145,51 +153,60 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
 
-  if (warp == 0) {
-    // ================================================================ TMA producer (both CTAs)
+  if (warp == 0 || warp >= kFirstExtraProducer) {
+    // ================================================================ TMA producers (both CTAs)
+    // kProducers warps share one ring.  The ring's stage sequence is fixed:
+    //   QK(0); then for every tile j: QK(j+1) (if any), V(j)
+    // and stage index i goes to producer i % kProducers and ring slot i % kStages, so each
+    // producer can derive the slot's use count (and the empty-barrier parity to wait for)
+    // from i alone.  One issuing warp sustains only a few million copies per second, well
+    // short of what the MMAs consume; several issuing warps multiply that rate.
+    const int pid = warp == 0 ? 0 : warp - kFirstExtraProducer + 1;
     if (elect_one() && n_tiles > 0) {
-      int s = 0;
-      uint32_t phase = 0;
       bool ok = true;
-      auto stage_begin = [&](uint32_t bytes_per_cta) -> uint32_t {
-        if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)))
-          return 0;
-        if (is_leader) mbar_arrive_expect_tx(smem_u32(&bars.full[s]), 2 * bytes_per_cta);
-        return mapa_shared(smem_u32(&bars.full[s]), leader);
-      };
-      auto stage_end = [&]() {
-        if (++s == kStages) { s = 0; phase ^= 1u; }
+      int i = 0;  // stage index in the sequence
+      // True if this producer owns stage i and its slot is free; `fb` is then the leader's
+      // full barrier of the slot (cluster address), armed for both CTAs' bytes.
+      uint32_t fb = 0;
+      auto own = [&](uint32_t bytes_per_cta) -> bool {
+        if (i % kProducers != pid) return false;
+        const int slot = i % kStages;
+        const uint32_t use = static_cast<uint32_t>(i / kStages);
+        if (use > 0 &&
+            !(ok = mbar_wait(smem_u32(&bars.empty[slot]), (use - 1) & 1u, kTimeoutStageFree, abort)))
+          return false;
+        if (is_leader) mbar_arrive_expect_tx(smem_u32(&bars.full[slot]), 2 * bytes_per_cta);
+        fb = mapa_shared(smem_u32(&bars.full[slot]), leader);
+        return true;
       };
       auto load_qk = [&](int j) {
         const int key0 = k_begin + j * kKeys;
         const int valid = min(kKeys, k_end - key0);
         const int n_qk = (valid + 15) & ~15;
         const int kbase = key0 + static_cast<int>(r) * (n_qk / 2);  // this CTA's half of the keys
-        XATTN_TRACE_POINT(0, j);
-        for (int c = 0; c < n_qk_chunks && ok; ++c) {
-          const uint32_t fb = stage_begin(16384 + 8192);
-          if (!ok) break;
-          const uint32_t st = smem_u32(stages + s * kStageBytes);
+        if (pid == 0) XATTN_TRACE_POINT(0, j);
+        for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
+          if (!own(16384 + 8192)) continue;
+          const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
           tma_load_3d_pair(st, &p.tq, fb, col0 + c * kChunk, row0, b);
           tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * kChunk, kbase, b);
-          stage_end();
         }
       };
       auto load_v = [&](int j) {
         const int key0 = k_begin + j * kKeys;
         const int valid = min(kKeys, k_end - key0);
         const int n_v = (valid + kVKeys - 1) / kVKeys;
-        XATTN_TRACE_POINT(1, j);
-        for (int v = 0; v < n_v && ok; ++v) {
-          const uint32_t fb = stage_begin(n_slabs * kVKeys * 128);
-          if (!ok) break;
-          const uint32_t st = smem_u32(stages + s * kStageBytes);
-          for (int i = 0; i < n_slabs; ++i) {
-            const int n = i / spi, jj = i % spi;
-            const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2) + jj * kChunk;
-            tma_load_3d_pair(st + i * (kVKeys * 128), &p.tv, fb, dim, key0 + v * kVKeys, b);
+        if (pid == 0) XATTN_TRACE_POINT(1, j);
+        for (int v = 0; v < n_v && ok; ++v, ++i) {
+          if (!own(n_slabs * kVKeys * 128)) continue;
+          const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
+          // one box of spi 32-column slabs per instruction: slab index (dim / 32) is the
+          // tensor map's third coordinate
+          for (int n = 0; n < n_instr; ++n) {
+            const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2);
+            tma_load_4d_pair(st + n * spi * (kVKeys * 128), &p.tv, fb, 0, key0 + v * kVKeys,
+                             dim / kChunk, b);
           }
-          stage_end();
         }
       };
       load_qk(0);
@@ -197,11 +214,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         if (j + 1 < n_tiles) load_qk(j + 1);
         load_v(j);
       }
-      // Drain: the pair MMA releases every stage it consumed; wait for the last ones so no
-      // load into this CTA's shared memory is still in flight at exit.
-      for (int i = 0; i < kStages; ++i) {
-        if (--s < 0) { s = kStages - 1; phase ^= 1u; }
-        mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, nullptr);
+      // Drain (producer 0): the pair MMA releases every stage it consumed; wait for the last
+      // use of every slot so no load into this CTA's shared memory is still in flight at exit.
+      if (pid == 0) {
+        for (int k = max(0, i - kStages); k < i; ++k)
+          mbar_wait(smem_u32(&bars.empty[k % kStages]), static_cast<uint32_t>(k / kStages) & 1u,
+                    kTimeoutDrain, nullptr);
       }
     }
   } else if (warp == 1) {
@@ -278,6 +296,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     }
   } else {
     // ================================================================ softmax / epilogue (both)
+    // warps 2 .. 2 + kSoftmaxThreads / 32 - 1
     const int sw = warp - 2;
     const int quad = warp & 3;
     const int grp = sw >> 2;
@@ -306,9 +325,11 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       tmem_ld32(t_row + kSCol + cbase, ra);
       tmem_ld32(t_row + kSCol + cbase + 32, rb);
       tmem_ld_wait();
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(18, j);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(lead_s_free);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
       // buffer of tile j: j % kXBufs, used for the (j / kXBufs)-th time
       const int xb_i = j % kXBufs;
       const uint32_t xb_par = static_cast<uint32_t>(j / kXBufs) & 1u;
@@ -362,6 +383,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int g = 1; g < kGroups; ++g) tmax = fmaxf(tmax, red[g][row]);
       named_bar_sync(2 + quad, 32 * kGroups);
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(15, j);
       m_true = fmaxf(m_true, tmax);
       float alpha = 1.f;
       if (j == 0) {
@@ -401,9 +423,11 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             make_uint4(q4[0], q4[1], q4[2], q4[3]);
       }
       l_run += lsum;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(16, j);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(17, j);
       if (lane == 0) mbar_arrive_remote(lead_p_full);
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
       if (kXBufs == 2 && j >= 1 && j + 1 < n_tiles) {

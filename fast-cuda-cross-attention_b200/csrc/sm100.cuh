@@ -55,11 +55,11 @@ __device__ __forceinline__ void record_status(int code) {
 // timer at named events of the first 8 CTAs and of CTAs 256..263 into g_trace[slot][event]
 // [tile].  In normal builds the macro expands to nothing.
 #ifdef XATTN_TRACE
-static __device__ unsigned long long g_trace[16][16][16];
+static __device__ unsigned long long g_trace[16][24][16];
 __device__ __forceinline__ void trace_point(int ev, int j) {
   const int cta = blockIdx.x;
   const int slot = cta < 8 ? cta : (cta >= 256 && cta < 264 ? cta - 248 : -1);
-  if (slot >= 0 && j < 16 && ev < 16) g_trace[slot][ev][j] = global_ns();
+  if (slot >= 0 && j < 16 && ev < 24) g_trace[slot][ev][j] = global_ns();
 }
 #define XATTN_TRACE_POINT(ev, j) ::xattn::trace_point((ev), (j))
 #else
@@ -85,9 +85,14 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 }
 
 // Arrive on an mbarrier that lives in another CTA of the cluster (address from mapa).
+// Default semantics (release at CTA scope), the form 2-SM tensor-core pipelines use to
+// signal a peer CTA.  Every use in this library either publishes nothing (TMEM already
+// read into registers, or a buffer whose readers finished) or follows a per-lane
+// fence.proxy.async for shared-memory data the tensor core reads next.  The
+// release.cluster form costs each arriving warp a cluster-scope fence, about 1 us on a
+// busy SM.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
@@ -212,6 +217,16 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap,
       "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
       "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Four-dimensional form of tma_load_3d_pair (a box of several 32-column slabs in one copy).
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster,
+                                                 int x, int y, int z, int w) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(tmap), "r"(bar_cluster), "r"(x), "r"(y), "r"(z), "r"(w)
       : "memory");
 }
 

@@ -174,6 +174,20 @@ int launch_fused_pair(const float* Q, const float* K, const float* V, float* out
   fused::Params p;
   if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D, fused::kKeys / 2, pair4::kVKeys))
     return XATTN_ERR_ARG;
+  {
+    // V as [B][D/32 slabs][Ni keys][32 columns]: one box holds all the 32-column slabs a CTA
+    // needs for one P.V instruction (dh / n_instr / 2 columns), so a V stage is one or two
+    // copies instead of up to six.
+    const int dh = D / 2;
+    const int spi = dh / (dh <= 256 ? 1 : 2) / 64;
+    const uint64_t dv[4] = {(uint64_t)fused::kChunk, (uint64_t)Ni, (uint64_t)D / fused::kChunk,
+                            (uint64_t)B};
+    const uint64_t sv[3] = {(uint64_t)D * 4, (uint64_t)fused::kChunk * 4, (uint64_t)Ni * D * 4};
+    const uint32_t bv[4] = {fused::kChunk, pair4::kVKeys, (uint32_t)spi, 1};
+    if (!encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, V, dv, sv, bv,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+      return XATTN_ERR_ARG;
+  }
   p.out = out;
   p.po = p.pm = p.pl = nullptr;
   p.batch = B;

@@ -1,0 +1,62 @@
+"""Run one cross-attention shape a few times on cuda:0 (for profilers and quick timing).
+
+    python fast-cuda-cross-attention_b200/run_case.py --batch 16 --n-latent 1024 \
+        --n-input 784 --dim 768 --iters 3 [--kernel 0|1|2] [--splits S]
+
+Inputs are seeded standard-normal fp32 tensors [B, N, D] created on the device; each
+iteration is one call of xattn.cross_attention (the fp32 entry, xattn_fp32).  --kernel
+selects the fused kernel (0 automatic, 1 two-CTA, 2 four-CTA pair) and --splits forces a
+key split count, through xattn_set_option.  Prints the mean time per call from CUDA events
+(not meaningful under a profiler) and checks the last output against a float64 reference
+on the first batch.
+"""
+
+import argparse
+import math
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--n-latent", type=int, default=1024)
+    ap.add_argument("--n-input", type=int, default=784)
+    ap.add_argument("--dim", type=int, default=768)
+    ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--kernel", type=int, default=0)
+    ap.add_argument("--splits", type=int, default=0)
+    a = ap.parse_args()
+
+    import torch
+
+    import xattn
+
+    xattn.set_option(xattn.OPT_KERNEL, a.kernel)
+    xattn.set_option(xattn.OPT_SPLITS, a.splits)
+    gen = torch.Generator(device="cuda").manual_seed(1234)
+    q = torch.randn(a.batch, a.n_latent, a.dim, device="cuda", generator=gen)
+    k = torch.randn(a.batch, a.n_input, a.dim, device="cuda", generator=gen)
+    v = torch.randn(a.batch, a.n_input, a.dim, device="cuda", generator=gen)
+    out = xattn.cross_attention(q, k, v)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.iters):
+        out = xattn.cross_attention(q, k, v)
+    e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / max(a.iters, 1)
+    ref = torch.softmax(q[0].double() @ k[0].double().T / math.sqrt(a.dim), -1) @ v[0].double()
+    err = (out[0].double() - ref).abs().max().item() / ref.abs().max().item()
+    tflops = xattn.flops(a.batch, a.n_latent, a.n_input, a.dim) / (ms * 1e-3) / 1e12
+    print(f"B={a.batch} Nl={a.n_latent} Ni={a.n_input} D={a.dim}: {ms * 1e3:.1f} us/call "
+          f"{tflops:.1f} TFLOP/s  rel err {err:.2e}  status {xattn.device_status()}")
+    if not err < 2e-3 or xattn.device_status() != 0:
+        sys.exit(1)
+
+
+if __name__ == "__main__":
+    main()
