@@ -1,0 +1,313 @@
+// Multi-head bf16 cross attention on tcgen05 (kind::f16: bf16 operands, fp32 accumulation).
+//
+// O[b, i, h*dh : (h+1)*dh] = softmax_j(Q_h[b, i] . K_h[b, j] / sqrt(dh)) V_h[b, j], with the
+// heads side by side in each row (row stride heads * dh), bf16 in and out.  This is the
+// per-head restatement of the upstream computation (generate_references.py:17-23 applied to
+// each head's columns); there is no upstream bf16 kernel.
+//
+// One CTA owns 128 query rows of one (batch, head); a head dimension of at most 128 leaves
+// TMEM room for two CTAs per SM (256 columns each: S for 64 keys at columns 0..63, O at
+// 128..128+dh), so the two CTAs' softmax and tensor phases overlap without any cross-CTA
+// protocol.  Per CTA:
+//   warp 0      TMA producer: Q once (resident), then K and V tiles of 64 keys through a
+//               3-stage ring in the order K(0), then per tile K(j+1), V(j)
+//   warp 1      MMA issuer: S = Q K^T (M=128, N=64, K=dh), O += P V (M=128, N=dh, K=64)
+//   warps 2..5  softmax, one query row per thread (warp w reads TMEM lanes 32*(w%4)..+31),
+//               then the epilogue
+// Operands in shared memory (128-byte swizzle, 64 bf16 per swizzle row):
+//   Q   K-major, ceil(dh/64) boxes of 128 rows x 64 columns
+//   K   K-major, boxes of 64 keys x 64 columns
+//   V   MN-major (rows are keys): the same boxes; the descriptor walks keys in 8-row groups
+//       (SBO 1024 B) and head columns in 64-wide groups (LBO = one box, 8 KB)
+//   P   K-major, 128 rows x 64 keys, written by the softmax warps (bf16)
+// A head dimension that is not a multiple of 64 loads the next head's (or out-of-range,
+// zero-filled) columns into the last box; the MMAs never read them.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "sm100.cuh"
+
+namespace xattn {
+namespace mha {
+
+constexpr int kRows = 128;
+constexpr int kKeys = 64;
+constexpr int kBoxCols = 64;                          // bf16 per 128-byte row
+constexpr int kMaxBoxes = 2;                          // head_dim <= 128
+constexpr int kQBytes = kMaxBoxes * kRows * 128;      // 32 KB
+constexpr int kBoxBytes = kKeys * 128;                // 8 KB: 64 keys x 64 columns
+constexpr int kStageBytes = kMaxBoxes * kBoxBytes;    // 16 KB: a K tile or a V tile
+constexpr int kStages = 3;
+constexpr int kPBytes = kRows * 128;                  // 16 KB
+constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kPBytes + 1024;
+constexpr int kThreads = 192;
+constexpr int kSoftmaxWarps = 4;
+constexpr int kTmemCols = 256;
+constexpr int kSCol = 0;
+constexpr int kOCol = 128;
+constexpr float kRescaleLog2 = 8.f;  // lazy rescale threshold (log2 units), as the fp32 kernels
+
+struct Params {
+  CUtensorMap tq, tk, tv;
+  __nv_bfloat16* out;
+  int heads, n_latent, n_input, dh, ld;  // ld = heads * dh elements per row
+  int n_row_blocks;
+  float scale_log2;
+};
+
+__host__ __device__ constexpr bool supports_dh(int dh) {
+  return dh == 64 || dh == 96 || dh == 128;
+}
+
+struct __align__(8) Barriers {
+  uint64_t q_full;
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t s_full;   // S of the current tile is in TMEM
+  uint64_t s_free;   // the softmax warps copied S out of TMEM
+  uint64_t p_full;   // P of the current tile is in shared memory
+  uint64_t pv_done;  // O += P V of the current tile completed (P buffer and O free)
+  uint64_t o_done;   // last P V completed
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&v);
+}
+
+__global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* qs = smem;
+  uint8_t* stages = smem + kQBytes;
+  uint8_t* ps = stages + kStages * kStageBytes;
+  __shared__ Barriers bars;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int rb = blockIdx.x % p.n_row_blocks;
+  const int bh = blockIdx.x / p.n_row_blocks;
+  const int h = bh % p.heads;
+  const int b = bh / p.heads;
+  const int row0 = rb * kRows;
+  const int col0 = h * p.dh;
+  const int n_tiles = (p.n_input + kKeys - 1) / kKeys;
+  const int n_boxes = (p.dh + kBoxCols - 1) / kBoxCols;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_u32(&bars.q_full), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bars.full[s]), 1);
+      mbar_init(smem_u32(&bars.empty[s]), 1);
+    }
+    mbar_init(smem_u32(&bars.s_full), 1);
+    mbar_init(smem_u32(&bars.s_free), kSoftmaxWarps);
+    mbar_init(smem_u32(&bars.p_full), kSoftmaxWarps);
+    mbar_init(smem_u32(&bars.pv_done), 1);
+    mbar_init(smem_u32(&bars.o_done), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 1 && lane == 0) {
+    tma_prefetch_desc(&p.tq);
+    tma_prefetch_desc(&p.tk);
+    tma_prefetch_desc(&p.tv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 0) {
+    // ============================================================== TMA producer
+    if (elect_one()) {
+      mbar_arrive_expect_tx(smem_u32(&bars.q_full), n_boxes * kRows * 128);
+      for (int c = 0; c < n_boxes; ++c)
+        tma_load_3d(smem_u32(qs + c * (kRows * 128)), &p.tq, smem_u32(&bars.q_full),
+                    col0 + c * kBoxCols, row0, b);
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      auto load = [&](const CUtensorMap* map, int tile) {
+        if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort))) return;
+        mbar_arrive_expect_tx(smem_u32(&bars.full[s]), n_boxes * kBoxBytes);
+        for (int c = 0; c < n_boxes; ++c)
+          tma_load_3d(smem_u32(stages + s * kStageBytes + c * kBoxBytes), map,
+                      smem_u32(&bars.full[s]), col0 + c * kBoxCols, tile * kKeys, b);
+        if (++s == kStages) { s = 0; phase ^= 1u; }
+      };
+      load(&p.tk, 0);
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) load(&p.tk, j + 1);
+        if (ok) load(&p.tv, j);
+      }
+      // every stage this CTA loaded is released by an MMA commit before the MMA warp
+      // finishes; wait for the last ones so no copy is in flight at exit
+      for (int i = 0; i < kStages; ++i) {
+        if (--s < 0) { s = kStages - 1; phase ^= 1u; }
+        mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, nullptr);
+      }
+      mbar_wait(smem_u32(&bars.q_full), 0, kTimeoutDrain, nullptr);
+    }
+  } else if (warp == 1) {
+    // ============================================================== MMA issuer
+    if (elect_one()) {
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = mbar_wait(smem_u32(&bars.q_full), 0, kTimeoutTmaFull, abort);
+      tc_fence_after();
+      const uint32_t idesc_qk = instr_desc(1, kRows, kKeys, false, false);
+      const uint32_t idesc_pv = instr_desc(1, kRows, p.dh, false, true);
+      const int ksteps_qk = p.dh / 16;
+      auto mma_qk = [&]() {
+        if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) return;
+        tc_fence_after();
+        const uint32_t st = smem_u32(stages + s * kStageBytes);
+        for (int ks = 0; ks < ksteps_qk; ++ks) {
+          const int c = ks >> 2, off = (ks & 3) * 32;
+          const uint64_t ad = smem_desc(smem_u32(qs) + c * (kRows * 128) + off, 16, 1024, kSw128);
+          const uint64_t bd = smem_desc(st + c * kBoxBytes + off, 16, 1024, kSw128);
+          mma_f16_ss(tmem + kSCol, ad, bd, idesc_qk, ks != 0);
+        }
+        mma_commit(smem_u32(&bars.empty[s]));
+        mma_commit(smem_u32(&bars.s_full));
+        if (++s == kStages) { s = 0; phase ^= 1u; }
+      };
+      if (ok && n_tiles > 0) mma_qk();
+      for (int j = 0; j < n_tiles && ok; ++j) {
+        if (j + 1 < n_tiles) {
+          if (!(ok = mbar_wait(smem_u32(&bars.s_free), j & 1, kTimeoutSoftmax, abort))) break;
+          tc_fence_after();
+          mma_qk();
+          if (!ok) break;
+        }
+        if (!(ok = mbar_wait(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
+        if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(stages + s * kStageBytes);
+#pragma unroll
+        for (int ks = 0; ks < kKeys / 16; ++ks) {
+          const uint64_t ad = smem_desc(smem_u32(ps) + ks * 32, 16, 1024, kSw128);
+          const uint64_t bd = smem_desc(st + ks * 2048, kBoxBytes, 1024, kSw128);
+          mma_f16_ss(tmem + kOCol, ad, bd, idesc_pv, (j | ks) != 0);
+        }
+        mma_commit(smem_u32(&bars.empty[s]));
+        mma_commit(smem_u32(&bars.pv_done));
+        if (++s == kStages) { s = 0; phase ^= 1u; }
+      }
+      mma_commit(smem_u32(&bars.o_done));
+    }
+  } else {
+    // ============================================================== softmax + epilogue
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
+    float m_run = -INFINITY;
+    float l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int valid = min(kKeys, p.n_input - j * kKeys);
+      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort))) break;
+      tc_fence_after();
+      uint32_t sa[32], sb[32];
+      tmem_ld32(t_row + kSCol, sa);
+      tmem_ld32(t_row + kSCol + 32, sb);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars.s_free));
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int k = 0; k < kKeys; ++k) {
+        uint32_t& rv = k < 32 ? sa[k] : sb[k - 32];
+        const float t = k < valid ? __uint_as_float(rv) * p.scale_log2 : -INFINITY;
+        tmax = fmaxf(tmax, t);
+        rv = __float_as_uint(t);
+      }
+      float alpha = 1.f;
+      if (j == 0) {
+        m_run = tmax;
+      } else if (tmax > m_run + kRescaleLog2) {
+        alpha = ex2_approx(m_run - tmax);
+        m_run = tmax;
+      }
+      // P buffer and O are in use by P V of the previous tile until it completes
+      if (j > 0 && !(ok = warp_mbar_wait(smem_u32(&bars.pv_done), (j - 1) & 1, kTimeoutMmaDone, abort)))
+        break;
+      if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        tc_fence_after();
+        for (int c = 0; c < p.dh / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_row + kOCol + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_row + kOCol + c * 32, o);
+        }
+        tmem_st_wait();
+      }
+      float lsum = 0.f;
+      uint8_t* prow = ps + row * 128;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds keys 8c .. 8c+7
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k0 = 8 * c + 2 * e;
+          const float x0 = __uint_as_float(k0 < 32 ? sa[k0] : sb[k0 - 32]);
+          const float x1 = __uint_as_float(k0 + 1 < 32 ? sa[k0 + 1] : sb[k0 + 1 - 32]);
+          const __nv_bfloat162 pb = __floats2bfloat162_rn(ex2_approx(x0 - m_run), ex2_approx(x1 - m_run));
+          // the row sum uses the rounded weights, as the P.V product does
+          const float2 pf = __bfloat1622float2(pb);
+          lsum += pf.x + pf.y;
+          w[e] = *reinterpret_cast<const uint32_t*>(&pb);
+        }
+        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      l_run = l_run * alpha + lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars.p_full));
+    }
+    // ---- epilogue: O / l -> bf16
+    if (ok && n_tiles > 0 && warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
+      tc_fence_after();
+      const int grow = row0 + row;
+      const float inv = 1.f / l_run;
+      __nv_bfloat16* dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.ld + col0;
+      for (int c = 0; c < p.dh / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(t_row + kOCol + c * 32, o);
+        tmem_ld_wait();
+        if (grow < p.n_latent) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            d4[i] = make_uint4(
+                pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
+                pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
+                pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
+                pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace mha
+}  // namespace xattn

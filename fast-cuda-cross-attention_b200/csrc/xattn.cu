@@ -21,6 +21,7 @@
 
 #include "fused_tf32.cuh"
 #include "fused_tf32_pair.cuh"
+#include "mha_bf16.cuh"
 #include "simt.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -71,6 +72,9 @@ int prepare_device(int* dev_out) {
     if (cudaFuncSetAttribute(pair4::fused_tf32_pair_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pair4::kSmemBytes) != cudaSuccess)
+      return XATTN_ERR_LAUNCH;
+    if (cudaFuncSetAttribute(mha::mha_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             mha::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
     st.init = true;
   }
@@ -485,6 +489,40 @@ extern "C" int xattn_lse_finalize(const float* ol, float* output, long long rows
   return set_error(cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
 }
 
+// Multi-head bf16 tensor-core kernel (mha_bf16.cuh): heads side by side in rows of
+// heads * head_dim elements.
+int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                    __nv_bfloat16* out, int B, int Nl, int Ni, int heads, int dh,
+                    cudaStream_t stream) {
+  mha::Params p;
+  const uint64_t ld = static_cast<uint64_t>(heads) * dh;
+  const uint64_t dq[3] = {ld, (uint64_t)Nl, (uint64_t)B};
+  const uint64_t sq[2] = {ld * 2, (uint64_t)Nl * ld * 2};
+  const uint64_t dk[3] = {ld, (uint64_t)Ni, (uint64_t)B};
+  const uint64_t sk[2] = {ld * 2, (uint64_t)Ni * ld * 2};
+  const uint32_t bq[3] = {mha::kBoxCols, mha::kRows, 1};
+  const uint32_t bk[3] = {mha::kBoxCols, mha::kKeys, 1};
+  if (!encode_tmap(&p.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, Q, dq, sq, bq,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap(&p.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, K, dk, sk, bk,
+                   CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dk, sk, bk,
+                   CU_TENSOR_MAP_SWIZZLE_128B))
+    return XATTN_ERR_ARG;
+  p.out = out;
+  p.heads = heads;
+  p.n_latent = Nl;
+  p.n_input = Ni;
+  p.dh = dh;
+  p.ld = static_cast<int>(ld);
+  p.n_row_blocks = (Nl + mha::kRows - 1) / mha::kRows;
+  p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(dh)));
+  const long long ctas = static_cast<long long>(B) * heads * p.n_row_blocks;
+  if (ctas > 0x7fffffffLL) return XATTN_ERR_ARG;
+  mha::mha_bf16_kernel<<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
 extern "C" int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                               const __nv_bfloat16* V, __nv_bfloat16* output, int batch_size,
                               int N_latent, int N_input, int heads, int head_dim,
@@ -495,6 +533,10 @@ extern "C" int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   int dev = 0;
   int rc = prepare_device(&dev);
   if (rc != XATTN_OK) return set_error(rc);
+  if (g_opt_path.load() != 2 && mha::supports_dh(head_dim) && aligned16(Q) && aligned16(K) &&
+      aligned16(V) && aligned16(output) && static_cast<long long>(heads) * head_dim <= 0x7fffffff)
+    return set_error(launch_mha_bf16(Q, K, V, output, batch_size, N_latent, N_input, heads,
+                                     head_dim, stream));
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(head_dim));
   return set_error(launch_simt<__nv_bfloat16, __nv_bfloat16>(
       Q, K, V, output, nullptr, nullptr, nullptr, batch_size, heads, N_latent, N_input, head_dim, 1,

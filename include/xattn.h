@@ -121,7 +121,9 @@ int xattn_lse_finalize(const float* ol, float* output, long long rows, int dim,
 
 /* Multi-head bf16 cross attention (no counterpart upstream): Q [B][N_latent][H*dh],
  * K, V [B][N_input][H*dh], heads contiguous inside each row, per-head scale 1/sqrt(dh),
- * fp32 accumulation, bf16 output [B][N_latent][H*dh].                                  */
+ * fp32 accumulation, bf16 output [B][N_latent][H*dh].  dh in {64, 96, 128} with 16-byte
+ * aligned pointers runs on the tcgen05 kind::f16 kernel; other head sizes on the generic
+ * CUDA-core kernel.                                                                    */
 int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                    __nv_bfloat16* output, int batch_size, int N_latent, int N_input,
                    int heads, int head_dim, cudaStream_t stream);

@@ -302,7 +302,11 @@ def test_wmma_fp16_entries(X, torch_cuda):
     assert_close(torch, torch.from_numpy(out2).cuda(), ref, TF32_TOL, "wmma-splitk")
 
 
-@pytest.mark.parametrize("shape", [(2, 128, 200, 8, 96), (1, 33, 65, 4, 64), (32, 1024, 784, 8, 96)])
+BF16_SHAPES = [(2, 128, 200, 8, 96), (1, 33, 65, 4, 64), (32, 1024, 784, 8, 96),
+               (3, 257, 1, 2, 128), (1, 130, 129, 3, 96), (2, 64, 1000, 1, 64), (1, 5, 70, 8, 32)]
+
+
+@pytest.mark.parametrize("shape", BF16_SHAPES)
 def test_bf16_multihead(X, torch_cuda, shape):
     torch = torch_cuda
     b, nl, ni, h, dh = shape
@@ -318,6 +322,52 @@ def test_bf16_multihead(X, torch_cuda, shape):
 
     ref = ref_attention(torch, heads(q, nl), heads(k, ni), heads(v, ni)).permute(0, 2, 1, 3)
     assert_close(torch, out.float(), ref.reshape(b, nl, h * dh), 2e-2, f"bf16 {shape}")
+
+
+def _bf16_heads_ref(torch, q, k, v, h):
+    b, nl, dm = q.shape
+    ni, dh = k.shape[1], dm // h
+
+    def heads(x, n):
+        return x.float().view(b, n, h, dh).permute(0, 2, 1, 3)
+
+    return ref_attention(torch, heads(q, nl), heads(k, ni), heads(v, ni)).permute(0, 2, 1, 3).reshape(b, nl, dm)
+
+
+@pytest.mark.parametrize("dh", [64, 96, 128])
+def test_bf16_rescale_every_tile(X, torch_cuda, dh):
+    """Logits that grow tile by tile (later keys have larger norms) make the running maximum
+    jump past the lazy-rescale threshold on every key tile, exercising the O rescale."""
+    torch = torch_cuda
+    b, nl, ni, h = 2, 192, 640, 2
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    q = (torch.randn(b, nl, h * dh, device="cuda", generator=gen) * 3).bfloat16()
+    growth = torch.arange(ni, device="cuda").div(64, rounding_mode="floor").float().mul(0.8).add(1)
+    k = (torch.randn(b, ni, h * dh, device="cuda", generator=gen) * growth[None, :, None]).bfloat16()
+    v = torch.randn(b, ni, h * dh, device="cuda", generator=gen).bfloat16()
+    out = X.cross_attention_bf16_mha(q, k, v, h)
+    torch.cuda.synchronize()
+    assert_close(torch, out.float(), _bf16_heads_ref(torch, q, k, v, h), 2e-2, f"bf16 rescale dh={dh}")
+    assert X.device_status() == 0
+
+
+def test_bf16_tensor_core_and_generic_kernels_agree(X, torch_cuda):
+    torch = torch_cuda
+    b, nl, ni, h, dh = 2, 200, 333, 8, 96
+    gen = torch.Generator(device="cuda").manual_seed(10)
+    q, k, v = (torch.randn(b, n, h * dh, device="cuda", generator=gen).bfloat16() for n in (nl, ni, ni))
+    fast = X.cross_attention_bf16_mha(q, k, v, h)
+    X.set_option(X.OPT_PATH, 2)
+    try:
+        generic = X.cross_attention_bf16_mha(q, k, v, h)
+    finally:
+        X.set_option(X.OPT_PATH, 0)
+    torch.cuda.synchronize()
+    ref = _bf16_heads_ref(torch, q, k, v, h)
+    scale = ref.abs().max().item()
+    assert (fast.float() - generic.float()).abs().max().item() <= 2e-2 * scale
+    assert_close(torch, fast.float(), ref, 2e-2, "bf16 tensor-core")
+    assert_close(torch, generic.float(), ref, 2e-2, "bf16 generic")
 
 
 # ----------------------------------------------------------------------- multi-GPU pieces on one GPU
