@@ -88,3 +88,46 @@ def dying_worker(rank, world, port, results):
             results.put((rank, f"error after {time.time() - t0:.1f}s: {type(exc).__name__}"))
     except Exception:
         results.put((rank, traceback.format_exc()))
+
+
+def nccl_split_worker(rank, world, port, results):
+    """One GPU rank of the NCCL N_input-split test (tests/test_multigpu.py).
+
+    Holds all of Q and the rank's slice of K/V, merges through
+    xattn.cross_attention_input_split, and reports its errors (relative to max|O_ref|)
+    against the single-GPU result and a float64 reference; then computes an N_latent row
+    shard with no collective and reports that error too."""
+    import datetime
+    import math
+
+    try:
+        import torch
+        import torch.distributed as dist
+
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        import xattn
+
+        b, nl, ni, d = 2, 200, 3000, 768
+        gen = torch.Generator(device="cuda").manual_seed(21)
+        q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+        lo, hi = xattn.shard_rows(ni, rank, world)
+        merged = xattn.cross_attention_input_split(q, k[:, lo:hi].contiguous(), v[:, lo:hi].contiguous())
+        full = xattn.cross_attention(q, k, v)
+        exact = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(d), -1) @ v.double()
+        scale = exact.abs().max().item()
+        r0, r1 = xattn.shard_rows(nl, rank, world)
+        rows = xattn.cross_attention(q[:, r0:r1].contiguous(), k, v)
+        torch.cuda.synchronize()
+        errs = ((merged - full).abs().max().item() / scale,
+                (merged.double() - exact).abs().max().item() / scale,
+                (rows.double() - exact[:, r0:r1]).abs().max().item() / scale)
+        status = xattn.device_status()
+        dist.barrier()
+        dist.destroy_process_group()
+        results.put((rank, errs, status, None))
+    except Exception:
+        results.put((rank, None, None, traceback.format_exc()))
