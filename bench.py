@@ -69,8 +69,9 @@ def measured_peaks():
 
 
 def committed_traffic():
-    """DRAM bytes per launch of the fused kernel from the committed ncu summary, or None."""
-    path = os.path.join(REPO, "profiles", "fused_tf32_C3_traffic.json")
+    """DRAM bytes per launch of the C3 kernel (fused_tf32_pair_kernel) from the committed
+    ncu summary, or None."""
+    path = os.path.join(REPO, "profiles", "fused_tf32_pair_C3_traffic.json")
     if os.path.exists(path):
         with open(path) as f:
             return json.load(f).get("dram_bytes_per_launch")
