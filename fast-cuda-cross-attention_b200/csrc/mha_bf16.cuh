@@ -6,9 +6,10 @@
 // each head's columns); there is no upstream bf16 kernel.
 //
 // One CTA owns 128 query rows of one (batch, head); a head dimension of at most 128 leaves
-// TMEM room for two CTAs per SM (256 columns each: S for 64 keys at columns 0..63, O at
-// 128..128+dh), so the two CTAs' softmax and tensor phases overlap without any cross-CTA
-// protocol.  Per CTA:
+// TMEM room for two CTAs per SM (256 columns each: two S tiles of 64 keys at columns 0..127,
+// O at 128..128+dh), so the two CTAs' softmax and tensor phases overlap without any cross-CTA
+// protocol.  S is double-buffered in TMEM (columns 0..63 and 64..127), so Q K^T of the next
+// tile never waits for the softmax warps to read the current one.  Per CTA:
 //   warp 0      TMA producer: Q once (resident), then K and V tiles of 64 keys through a
 //               3-stage ring in the order K(0), then per tile K(j+1), V(j)
 //   warp 1      MMA issuer: S = Q K^T (M=128, N=64, K=dh), O += P V (M=128, N=dh, K=64)
@@ -64,12 +65,18 @@ struct __align__(8) Barriers {
   uint64_t q_full;
   uint64_t full[kStages];
   uint64_t empty[kStages];
-  uint64_t s_full;   // S of the current tile is in TMEM
-  uint64_t s_free;   // the softmax warps copied S out of TMEM
+  uint64_t s_full[2];  // S buffer b holds the scores of tile j (j % 2 == b)
+  uint64_t s_free[2];  // the softmax warps copied S buffer b out of TMEM
   uint64_t p_full;   // P of the current tile is in shared memory
   uint64_t pv_done;  // O += P V of the current tile completed (P buffer and O free)
   uint64_t o_done;   // last P V completed
 };
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
@@ -105,8 +112,10 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
-    mbar_init(smem_u32(&bars.s_full), 1);
-    mbar_init(smem_u32(&bars.s_free), kSoftmaxWarps);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars.s_full[i]), 1);
+      mbar_init(smem_u32(&bars.s_free[i]), kSoftmaxWarps);
+    }
     mbar_init(smem_u32(&bars.p_full), kSoftmaxWarps);
     mbar_init(smem_u32(&bars.pv_done), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
@@ -168,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       const uint32_t idesc_qk = instr_desc(1, kRows, kKeys, false, false);
       const uint32_t idesc_pv = instr_desc(1, kRows, p.dh, false, true);
       const int ksteps_qk = p.dh / 16;
-      auto mma_qk = [&]() {
+      auto mma_qk = [&](int t) {  // S of tile t into buffer t % 2
         if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) return;
         tc_fence_after();
         const uint32_t st = smem_u32(stages + s * kStageBytes);
@@ -176,18 +185,22 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           const int c = ks >> 2, off = (ks & 3) * 32;
           const uint64_t ad = smem_desc(smem_u32(qs) + c * (kRows * 128) + off, 16, 1024, kSw128);
           const uint64_t bd = smem_desc(st + c * kBoxBytes + off, 16, 1024, kSw128);
-          mma_f16_ss(tmem + kSCol, ad, bd, idesc_qk, ks != 0);
+          mma_f16_ss(tmem + kSCol + (t & 1) * kKeys, ad, bd, idesc_qk, ks != 0);
         }
         mma_commit(smem_u32(&bars.empty[s]));
-        mma_commit(smem_u32(&bars.s_full));
+        mma_commit(smem_u32(&bars.s_full[t & 1]));
         if (++s == kStages) { s = 0; phase ^= 1u; }
       };
-      if (ok && n_tiles > 0) mma_qk();
+      if (ok && n_tiles > 0) mma_qk(0);
       for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles) {
-          if (!(ok = mbar_wait(smem_u32(&bars.s_free), j & 1, kTimeoutSoftmax, abort))) break;
+        const int t = j + 1;
+        if (t < n_tiles) {
+          // buffer t % 2 last held tile t - 2: wait until the softmax warps read it
+          if (t >= 2 && !(ok = mbar_wait(smem_u32(&bars.s_free[t & 1]), ((t >> 1) - 1) & 1,
+                                         kTimeoutSoftmax, abort)))
+            break;
           tc_fence_after();
-          mma_qk();
+          mma_qk(t);
           if (!ok) break;
         }
         if (!(ok = mbar_wait(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
@@ -216,23 +229,39 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       const int valid = min(kKeys, p.n_input - j * kKeys);
-      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort))) break;
+      const int sbuf = j & 1;
+      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full[sbuf]), (j >> 1) & 1, kTimeoutMmaDone, abort)))
+        break;
       tc_fence_after();
-      uint32_t sa[32], sb[32];
-      tmem_ld32(t_row + kSCol, sa);
-      tmem_ld32(t_row + kSCol + 32, sb);
-      tmem_ld_wait();
+      float x[kKeys];  // raw scores of this row
+      {
+        uint32_t sa[32], sb[32];
+        tmem_ld32(t_row + kSCol + sbuf * kKeys, sa);
+        tmem_ld32(t_row + kSCol + sbuf * kKeys + 32, sb);
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          x[k] = __uint_as_float(sa[k]);
+          x[k + 32] = __uint_as_float(sb[k]);
+        }
+      }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars.s_free));
-      float tmax = -INFINITY;
+      if (lane == 0) mbar_arrive(smem_u32(&bars.s_free[sbuf]));
+      if (valid < kKeys) {  // ragged last tile: keys past N_input get weight 0
 #pragma unroll
-      for (int k = 0; k < kKeys; ++k) {
-        uint32_t& rv = k < 32 ? sa[k] : sb[k - 32];
-        const float t = k < valid ? __uint_as_float(rv) * p.scale_log2 : -INFINITY;
-        tmax = fmaxf(tmax, t);
-        rv = __float_as_uint(t);
+        for (int k = 0; k < kKeys; ++k) x[k] = k < valid ? x[k] : -INFINITY;
       }
+      // row maximum of the raw scores (the scale is positive), four independent chains
+      float mx[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        mx[c] = x[16 * c];
+#pragma unroll
+        for (int k = 1; k < 15; k += 2) mx[c] = fmax3(mx[c], x[16 * c + k], x[16 * c + k + 1]);
+        mx[c] = fmaxf(mx[c], x[16 * c + 15]);
+      }
+      const float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * p.scale_log2;
       float alpha = 1.f;
       if (j == 0) {
         m_run = tmax;
@@ -255,6 +284,10 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         }
         tmem_st_wait();
       }
+      // weights 2^(x * scale_log2 - m): one FFMA and one ex2 per score.  The row sum adds the
+      // bf16-rounded weights the P.V product uses, so each output row is an exact weighted
+      // mean of V (summing the unrounded weights doubles the error when a few keys dominate)
+      const float neg_m = -m_run;
       float lsum = 0.f;
       uint8_t* prow = ps + row * 128;
 #pragma unroll
@@ -263,13 +296,10 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int k0 = 8 * c + 2 * e;
-          const float x0 = __uint_as_float(k0 < 32 ? sa[k0] : sb[k0 - 32]);
-          const float x1 = __uint_as_float(k0 + 1 < 32 ? sa[k0 + 1] : sb[k0 + 1 - 32]);
-          const __nv_bfloat162 pb = __floats2bfloat162_rn(ex2_approx(x0 - m_run), ex2_approx(x1 - m_run));
-          // the row sum uses the rounded weights, as the P.V product does
-          const float2 pf = __bfloat1622float2(pb);
-          lsum += pf.x + pf.y;
-          w[e] = *reinterpret_cast<const uint32_t*>(&pb);
+          const float p0 = ex2_approx(fmaf(x[k0], p.scale_log2, neg_m));
+          const float p1 = ex2_approx(fmaf(x[k0 + 1], p.scale_log2, neg_m));
+          w[e] = pack_bf16x2(p0, p1);
+          lsum += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xffff0000u);
         }
         *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
