@@ -20,9 +20,18 @@
 //   K   K-major, boxes of 64 keys x 64 columns
 //   V   MN-major (rows are keys): the same boxes; the descriptor walks keys in 8-row groups
 //       (SBO 1024 B) and head columns in 64-wide groups (LBO = one box, 8 KB)
-//   P   K-major, 128 rows x 64 keys, written by the softmax warps (bf16)
+//   P   K-major, 128 rows x 64 keys, written by the softmax warps (bf16), two buffers so the
+//       softmax of tile j+1 does not wait for O += P V of tile j
+// The barriers live at the end of the dynamic shared memory: with no static shared memory
+// the dynamic region starts 1024-byte aligned (checked at run time), which leaves room for
+// two CTAs of 112 KB per SM.
 // A head dimension that is not a multiple of 64 loads the next head's (or out-of-range,
 // zero-filled) columns into the last box; the MMAs never read them.
+// Row sums on the tensor core (kTcSum, d <= 112): with each P.V step the MMA issuer also
+// multiplies P by an all-ones B operand (N = 16), accumulating l = sum_k P[r, k] of the
+// bf16-rounded weights into TMEM columns 128+d .. 143+d; the softmax warps then do no
+// per-score summation.  The ones operand is a single 128-byte no-swizzle core matrix read
+// with zero strides, valid because every element of the operand is the same.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -40,8 +49,11 @@ constexpr int kQBytes = kMaxBoxes * kRows * 128;      // 32 KB
 constexpr int kBoxBytes = kKeys * 128;                // 8 KB: 64 keys x 64 columns
 constexpr int kStageBytes = kMaxBoxes * kBoxBytes;    // 16 KB: a K tile or a V tile
 constexpr int kStages = 3;
-constexpr int kPBytes = kRows * 128;                  // 16 KB
-constexpr int kSmemBytes = kQBytes + kStages * kStageBytes + kPBytes + 1024;
+constexpr int kPBytes = kRows * 128;                  // 16 KB per buffer
+constexpr int kPBufs = 2;
+constexpr int kBarOffset = kQBytes + kStages * kStageBytes + kPBufs * kPBytes;
+constexpr int kOnesOffset = kBarOffset + 256;   // 8 rows x 16 B of bf16 ones
+constexpr int kSmemBytes = kOnesOffset + 128;
 constexpr int kThreads = 192;
 constexpr int kSoftmaxWarps = 4;
 constexpr int kTmemCols = 256;
@@ -67,10 +79,13 @@ struct __align__(8) Barriers {
   uint64_t empty[kStages];
   uint64_t s_full[2];  // S buffer b holds the scores of tile j (j % 2 == b)
   uint64_t s_free[2];  // the softmax warps copied S buffer b out of TMEM
-  uint64_t p_full;   // P of the current tile is in shared memory
-  uint64_t pv_done;  // O += P V of the current tile completed (P buffer and O free)
-  uint64_t o_done;   // last P V completed
+  uint64_t p_full;      // P of the current tile is in shared memory
+  uint64_t pv_done[2];  // O += P V of a tile using P buffer b completed (buffer free, O current)
+  uint64_t o_done;      // last P V completed
+  uint32_t tmem_slot;
+  int abort_flag;
 };
+static_assert(sizeof(Barriers) <= 256, "barrier block exceeds its reserved bytes");
 
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float r;
@@ -83,16 +98,24 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
+__host__ __device__ constexpr bool tc_sum_for(int dh) { return dh <= 112; }
+
+template <bool kTcSum>
 __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_constant__ Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  // swizzled TMA boxes and UMMA descriptors need 1024-byte alignment; the kernel has no
+  // static shared memory, so the dynamic region starts at the window base.  Checked anyway:
+  // a misaligned region records a status code and the CTA does nothing (uniform exit).
+  if ((smem_u32(smem) & 1023u) != 0) {
+    if (threadIdx.x == 0) record_status(kMisalignedSmem);
+    return;
+  }
   uint8_t* qs = smem;
   uint8_t* stages = smem + kQBytes;
   uint8_t* ps = stages + kStages * kStageBytes;
-  __shared__ Barriers bars;
-  __shared__ uint32_t tmem_slot;
-  __shared__ int abort_flag;
+  Barriers& bars = *reinterpret_cast<Barriers*>(smem + kBarOffset);
+  uint32_t& tmem_slot = bars.tmem_slot;
+  int& abort_flag = bars.abort_flag;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -104,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   const int col0 = h * p.dh;
   const int n_tiles = (p.n_input + kKeys - 1) / kKeys;
   const int n_boxes = (p.dh + kBoxCols - 1) / kBoxCols;
+  if (threadIdx.x == 0) XATTN_TRACE_POINT(14, 0);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -117,13 +141,18 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       mbar_init(smem_u32(&bars.s_free[i]), kSoftmaxWarps);
     }
     mbar_init(smem_u32(&bars.p_full), kSoftmaxWarps);
-    mbar_init(smem_u32(&bars.pv_done), 1);
+    mbar_init(smem_u32(&bars.pv_done[0]), 1);
+    mbar_init(smem_u32(&bars.pv_done[1]), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
     fence_mbar_init();
   }
   if (warp == 0) {
     tmem_alloc(smem_u32(&tmem_slot), kTmemCols);
     tmem_relinquish();
+  }
+  if (kTcSum && warp == 2) {  // the ones operand: 64 bf16 of 1.0, for the tensor core
+    reinterpret_cast<uint32_t*>(smem + kOnesOffset)[lane] = 0x3F803F80u;
+    fence_proxy_async_smem();
   }
   if (warp == 1 && lane == 0) {
     tma_prefetch_desc(&p.tq);
@@ -157,7 +186,9 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       load(&p.tk, 0);
       for (int j = 0; j < n_tiles && ok; ++j) {
         if (j + 1 < n_tiles) load(&p.tk, j + 1);
+        XATTN_TRACE_POINT(0, j + 1);
         if (ok) load(&p.tv, j);
+        XATTN_TRACE_POINT(1, j);
       }
       // every stage this CTA loaded is released by an MMA commit before the MMA warp
       // finishes; wait for the last ones so no copy is in flight at exit
@@ -176,6 +207,8 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       tc_fence_after();
       const uint32_t idesc_qk = instr_desc(1, kRows, kKeys, false, false);
       const uint32_t idesc_pv = instr_desc(1, kRows, p.dh, false, true);
+      const uint32_t idesc_sum = instr_desc(1, kRows, 16, false, false);
+      const uint64_t ones_desc = smem_desc(smem_u32(smem + kOnesOffset), 0, 0, kSwNone);
       const int ksteps_qk = p.dh / 16;
       auto mma_qk = [&](int t) {  // S of tile t into buffer t % 2
         if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) return;
@@ -189,6 +222,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         }
         mma_commit(smem_u32(&bars.empty[s]));
         mma_commit(smem_u32(&bars.s_full[t & 1]));
+        XATTN_TRACE_POINT(2, t);
         if (++s == kStages) { s = 0; phase ^= 1u; }
       };
       if (ok && n_tiles > 0) mma_qk(0);
@@ -204,17 +238,20 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           if (!ok) break;
         }
         if (!(ok = mbar_wait(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
+        XATTN_TRACE_POINT(3, j);
         if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
         tc_fence_after();
         const uint32_t st = smem_u32(stages + s * kStageBytes);
 #pragma unroll
         for (int ks = 0; ks < kKeys / 16; ++ks) {
-          const uint64_t ad = smem_desc(smem_u32(ps) + ks * 32, 16, 1024, kSw128);
+          const uint64_t ad = smem_desc(smem_u32(ps + (j & 1) * kPBytes) + ks * 32, 16, 1024, kSw128);
           const uint64_t bd = smem_desc(st + ks * 2048, kBoxBytes, 1024, kSw128);
           mma_f16_ss(tmem + kOCol, ad, bd, idesc_pv, (j | ks) != 0);
+          if (kTcSum) mma_f16_ss(tmem + kOCol + p.dh, ad, ones_desc, idesc_sum, (j | ks) != 0);
         }
         mma_commit(smem_u32(&bars.empty[s]));
-        mma_commit(smem_u32(&bars.pv_done));
+        mma_commit(smem_u32(&bars.pv_done[j & 1]));
+        XATTN_TRACE_POINT(4, j);
         if (++s == kStages) { s = 0; phase ^= 1u; }
       }
       mma_commit(smem_u32(&bars.o_done));
@@ -232,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       const int sbuf = j & 1;
       if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full[sbuf]), (j >> 1) & 1, kTimeoutMmaDone, abort)))
         break;
+      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(6, j);
       tc_fence_after();
       float x[kKeys];  // raw scores of this row
       {
@@ -248,6 +286,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars.s_free[sbuf]));
+      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(7, j);
       if (valid < kKeys) {  // ragged last tile: keys past N_input get weight 0
 #pragma unroll
         for (int k = 0; k < kKeys; ++k) x[k] = k < valid ? x[k] : -INFINITY;
@@ -269,10 +308,16 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         alpha = ex2_approx(m_run - tmax);
         m_run = tmax;
       }
-      // P buffer and O are in use by P V of the previous tile until it completes
-      if (j > 0 && !(ok = warp_mbar_wait(smem_u32(&bars.pv_done), (j - 1) & 1, kTimeoutMmaDone, abort)))
+      // P buffer j % 2 is read by P V of tile j - 2 until that completes
+      if (j >= 2 && !(ok = warp_mbar_wait(smem_u32(&bars.pv_done[j & 1]), ((j >> 1) - 1) & 1,
+                                         kTimeoutMmaDone, abort)))
         break;
+      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(8, j);
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        // rescaling O needs every earlier P V complete: the last one is tile j - 1
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
+                                  kTimeoutMmaDone, abort)))
+          break;
         tc_fence_after();
         for (int c = 0; c < p.dh / 32; ++c) {
           uint32_t o[32];
@@ -282,6 +327,14 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
           tmem_st32(t_row + kOCol + c * 32, o);
         }
+        if (kTcSum) {  // the row-sum columns scale with O
+          uint32_t o[16];
+          tmem_ld16(t_row + kOCol + p.dh, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st16(t_row + kOCol + p.dh, o);
+        }
         tmem_st_wait();
       }
       // weights 2^(x * scale_log2 - m): one FFMA and one ex2 per score.  The row sum adds the
@@ -289,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       // mean of V (summing the unrounded weights doubles the error when a few keys dominate)
       const float neg_m = -m_run;
       float lsum = 0.f;
-      uint8_t* prow = ps + row * 128;
+      uint8_t* prow = ps + (j & 1) * kPBytes + row * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds keys 8c .. 8c+7
         uint32_t w[4];
@@ -299,7 +352,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           const float p0 = ex2_approx(fmaf(x[k0], p.scale_log2, neg_m));
           const float p1 = ex2_approx(fmaf(x[k0 + 1], p.scale_log2, neg_m));
           w[e] = pack_bf16x2(p0, p1);
-          lsum += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xffff0000u);
+          if (!kTcSum) lsum += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xffff0000u);
         }
         *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
@@ -308,12 +361,20 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars.p_full));
+      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(10, j);
     }
     // ---- epilogue: O / l -> bf16
     if (ok && n_tiles > 0 && warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
       tc_fence_after();
       const int grow = row0 + row;
-      const float inv = 1.f / l_run;
+      float l_tot = l_run;
+      if (kTcSum) {
+        uint32_t lr[16];
+        tmem_ld16(t_row + kOCol + p.dh, lr);
+        tmem_ld_wait();
+        l_tot = __uint_as_float(lr[0]);
+      }
+      const float inv = 1.f / l_tot;
       __nv_bfloat16* dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.ld + col0;
       for (int c = 0; c < p.dh / 32; ++c) {
         uint32_t o[32];
@@ -336,6 +397,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (threadIdx.x == 0) XATTN_TRACE_POINT(13, 0);
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 

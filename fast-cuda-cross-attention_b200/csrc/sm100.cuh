@@ -33,6 +33,7 @@ enum StatusCode : int {
   kTimeoutExchange = 5,
   kTimeoutPeer = 6,
   kTimeoutDrain = 7,
+  kMisalignedSmem = 8,  // dynamic shared memory not 1024-byte aligned (kernel did nothing)
   kTimeoutInjected = 99,
 };
 
@@ -131,6 +132,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
   while (true) {
     if (kCluster ? mbar_try_wait_cluster(bar, parity) : mbar_try_wait(bar, parity)) return true;
     if ((++spins & 63u) == 0) {
+      if (abort != nullptr && *abort) return false;
+      if (global_ns() - t0 > g_wait_ns) {
+        record_status(code);
+        if (abort != nullptr) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// Non-suspending probe of an mbarrier phase (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait that polls with test_wait instead of suspending in try_wait: for a single
+// issuing thread on the critical path, where the wake-up of a suspended try_wait (a few
+// hundred ns after the phase completes) would delay the next tensor-core instruction.
+__device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, int code,
+                                               volatile int* abort) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
       if (abort != nullptr && *abort) return false;
       if (global_ns() - t0 > g_wait_ns) {
         record_status(code);

@@ -73,8 +73,10 @@ int prepare_device(int* dev_out) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pair4::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
-    if (cudaFuncSetAttribute(mha::mha_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             mha::kSmemBytes) != cudaSuccess)
+    if (cudaFuncSetAttribute(mha::mha_bf16_kernel<true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, mha::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(mha::mha_bf16_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, mha::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
     st.init = true;
   }
@@ -519,7 +521,10 @@ int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_b
   p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(dh)));
   const long long ctas = static_cast<long long>(B) * heads * p.n_row_blocks;
   if (ctas > 0x7fffffffLL) return XATTN_ERR_ARG;
-  mha::mha_bf16_kernel<<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
+  if (mha::tc_sum_for(dh))
+    mha::mha_bf16_kernel<true><<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
+  else
+    mha::mha_bf16_kernel<false><<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 
