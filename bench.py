@@ -85,7 +85,7 @@ class ClockSampler:
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, pci_bus_id, period=0.01):
+    def __init__(self, pci_bus_id, period=0.002):
         self.samples, self.period, self.ok = [], period, False
         self._stop = threading.Event()
         try:
@@ -104,8 +104,9 @@ class ClockSampler:
         while not self._stop.is_set():
             try:
                 sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                t = time.time()
                 reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((time.time(), sm, reasons))
+                self.samples.append((t, sm, reasons))
             except Exception:
                 pass
             time.sleep(self.period)

@@ -180,5 +180,20 @@ __global__ void __launch_bounds__(128) lse_pack_kernel(const float* __restrict__
   if (lane == 0) ol[r * (dim + 1) + dim] = pl[r];
 }
 
+// Widen fp16 to fp32 (exact: every fp16 value is representable in fp32, and in TF32), 8
+// elements per thread per step.  n8 = number of 8-element groups; in and out 16-byte aligned.
+__global__ void __launch_bounds__(256) widen_half_kernel(const uint4* __restrict__ in,
+                                                         float4* __restrict__ out, long long n8) {
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const uint4 v = in[i];
+    const __half2* h = reinterpret_cast<const __half2*>(&v);
+    const float2 a = __half22float2(h[0]), b = __half22float2(h[1]);
+    const float2 c = __half22float2(h[2]), d = __half22float2(h[3]);
+    out[2 * i] = make_float4(a.x, a.y, b.x, b.y);
+    out[2 * i + 1] = make_float4(c.x, c.y, d.x, d.y);
+  }
+}
+
 }  // namespace simt
 }  // namespace xattn

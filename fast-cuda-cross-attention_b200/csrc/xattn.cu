@@ -17,6 +17,7 @@
 #include <cstdlib>
 #include <map>
 #include <mutex>
+#include <tuple>
 #include <utility>
 
 #include "fused_tf32.cuh"
@@ -144,10 +145,20 @@ bool make_fp32_maps(fused::Params& p, const float* Q, const float* K, const floa
                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
+// Score scale and TF32 compensation of a launch.  score_scale < 0 means 1/sqrt(D); exact
+// inputs (already representable in TF32, e.g. widened fp16) take no truncation compensation.
+void set_scale(fused::Params& p, int D, float score_scale, bool exact_inputs) {
+  const double sc = score_scale < 0.f ? 1.0 / std::sqrt(static_cast<double>(D)) : score_scale;
+  const bool comp = !exact_inputs && g_opt_tf32_comp.load() != 0;
+  p.scale_log2 = static_cast<float>(kLog2e * sc * (comp ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
+  p.out_comp = comp ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+}
+
 // Launch the fused kernel.  split_mode = 0: normalised output `out`; 1: partials.
 int launch_fused(const float* Q, const float* K, const float* V, float* out, float* po,
                  float* pm, float* pl, int B, int Nl, int Ni, int D, int num_splits,
-                 int split_chunk, int split_mode, cudaStream_t stream) {
+                 int split_chunk, int split_mode, cudaStream_t stream, float score_scale = -1.f,
+                 bool exact_inputs = false) {
   fused::Params p;
   if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D)) return XATTN_ERR_ARG;
   p.out = out;
@@ -163,10 +174,7 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
   p.num_splits = num_splits;
   p.split_chunk = split_chunk;
   p.split_mode = split_mode;
-  const bool comp = g_opt_tf32_comp.load() != 0;
-  p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(D)) *
-                                    (comp ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
-  p.out_comp = comp ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+  set_scale(p, D, score_scale, exact_inputs);
   const long long items = static_cast<long long>(B) * p.n_row_blocks * num_splits;
   if (items * 2 > 0x7fffffffLL) return XATTN_ERR_ARG;
   fused::fused_tf32_kernel<<<static_cast<unsigned>(items * 2), fused::kThreads, fused::kSmemBytes,
@@ -176,7 +184,8 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
 
 // Four-CTA pair kernel, normalised output (fused_tf32_pair.cuh).
 int launch_fused_pair(const float* Q, const float* K, const float* V, float* out, int B, int Nl,
-                      int Ni, int D, cudaStream_t stream) {
+                      int Ni, int D, cudaStream_t stream, float score_scale = -1.f,
+                      bool exact_inputs = false) {
   fused::Params p;
   if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D, fused::kKeys / 2, pair4::kVKeys))
     return XATTN_ERR_ARG;
@@ -205,10 +214,7 @@ int launch_fused_pair(const float* Q, const float* K, const float* V, float* out
   p.num_splits = 1;
   p.split_chunk = Ni;
   p.split_mode = 0;
-  const bool comp = g_opt_tf32_comp.load() != 0;
-  p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(D)) *
-                                    (comp ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
-  p.out_comp = comp ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+  set_scale(p, D, score_scale, exact_inputs);
   const long long items = static_cast<long long>(B) * p.n_row_blocks;
   if (items * 4 > 0x7fffffffLL) return XATTN_ERR_ARG;
   pair4::fused_tf32_pair_kernel<<<static_cast<unsigned>(items * 4), pair4::kThreads,
@@ -363,6 +369,78 @@ int run_splitk(const float* Q, const float* K, const float* V, float* O, float* 
   return set_error(launch_combine(po, pm, pl, O, static_cast<long long>(B) * Nl, D, S, stream));
 }
 
+// fp16 entries (upstream kernel_wmma.cu / kernel_wmma_splitk.cu; Q pre-scaled by 1/sqrt(D)
+// on the host, cuda_wrappers.py:635-640).  Every fp16 value is exactly representable in
+// TF32, so the inputs are widened to fp32 in the library workspace and the tcgen05 TF32
+// kernels compute exactly the products an fp16 MMA would (fp32 accumulation), with score
+// scale 1 and no truncation compensation.  S = 0: the plain entry (automatic kernel and key
+// split); S > 0: the split entry, partials into the caller's po/pm/pl with the upstream
+// chunk of max(16, round_up(ceil(Ni/S), 16)) keys (kernel_wmma_splitk.cu:52).  Shapes the
+// tensor-core kernels do not take run the generic kernel on the fp16 data directly.
+int run_half(const __half* Q, const __half* K, const __half* V, float* O, float* po, float* pm,
+             float* pl, int B, int Nl, int Ni, int D, int S, cudaStream_t stream) {
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return rc;
+  const int chunk16 = S > 0 ? std::max(16, ((Ni + S - 1) / S + 15) / 16 * 16) : Ni;
+  const bool tc = g_opt_path.load() != 2 && D % 64 == 0 && D >= 64 && D <= 2 * fused::kMaxDh &&
+                  aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O) &&
+                  (S == 0 || aligned16(po));
+  if (!tc) {
+    if (S == 0)
+      return launch_simt<__half, float>(Q, K, V, O, nullptr, nullptr, nullptr, B, 1, Nl, Ni, D, 1,
+                                        Ni, 0, kLog2e, stream);
+    rc = launch_simt<__half, float>(Q, K, V, nullptr, po, pm, pl, B, 1, Nl, Ni, D, S, chunk16, 1,
+                                    kLog2e, stream);
+    if (rc != XATTN_OK) return rc;
+    return launch_combine(po, pm, pl, O, static_cast<long long>(B) * Nl, D, S, stream);
+  }
+  // plan first, so one workspace request covers the widened inputs and any split partials
+  const bool pair = S == 0 && g_opt_splits.load() <= 0 && use_pair_kernel(dev, B, Nl, D);
+  int splits = 1, chunk = Ni;
+  if (S == 0 && !pair) plan_splits(dev, B, Nl, Ni, g_opt_path.load(), &splits, &chunk);
+  const size_t nq = static_cast<size_t>(B) * Nl * D, nk = static_cast<size_t>(B) * Ni * D;
+  const size_t rows = static_cast<size_t>(B) * Nl;
+  const size_t po_elems = splits > 1 ? rows * splits * D : 0;
+  const size_t ml_elems = splits > 1 ? rows * splits : 0;
+  // each region rounded to 64 floats (256 B) so every base stays 16-byte aligned
+  auto r64 = [](size_t n) { return (n + 63) / 64 * 64; };
+  float* ws = static_cast<float*>(workspace(
+      dev, stream, (r64(nq) + 2 * r64(nk) + r64(po_elems) + 2 * r64(ml_elems)) * sizeof(float)));
+  if (ws == nullptr) return XATTN_ERR_NOMEM;
+  float* q32 = ws;
+  float* k32 = q32 + r64(nq);
+  float* v32 = k32 + r64(nk);
+  float* wpo = v32 + r64(nk);
+  float* wpm = wpo + r64(po_elems);
+  float* wpl = wpm + r64(ml_elems);
+  const int sms = sm_count(dev);
+  for (auto [src, dst, n] : {std::tuple<const __half*, float*, size_t>{Q, q32, nq},
+                             {K, k32, nk}, {V, v32, nk}}) {
+    if (n == 0) continue;
+    // D % 64 == 0, so every tensor holds a whole number of 8-element groups
+    const long long n8 = static_cast<long long>(n / 8);
+    const unsigned blocks = static_cast<unsigned>(std::min<long long>((n8 + 255) / 256, sms * 8LL));
+    simt::widen_half_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const uint4*>(src),
+                                                        reinterpret_cast<float4*>(dst), n8);
+  }
+  if (cudaPeekAtLastError() != cudaSuccess) return XATTN_ERR_LAUNCH;
+  if (S > 0) {
+    rc = launch_fused(q32, k32, v32, nullptr, po, pm, pl, B, Nl, Ni, D, S, chunk16, 1, stream,
+                      1.f, true);
+    if (rc != XATTN_OK) return rc;
+    return launch_combine(po, pm, pl, O, static_cast<long long>(rows), D, S, stream);
+  }
+  if (pair) return launch_fused_pair(q32, k32, v32, O, B, Nl, Ni, D, stream, 1.f, true);
+  if (splits == 1)
+    return launch_fused(q32, k32, v32, O, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni, 0,
+                        stream, 1.f, true);
+  rc = launch_fused(q32, k32, v32, nullptr, wpo, wpm, wpl, B, Nl, Ni, D, splits, chunk, 1, stream,
+                    1.f, true);
+  if (rc != XATTN_OK) return rc;
+  return launch_combine(wpo, wpm, wpl, O, static_cast<long long>(rows), D, splits, stream);
+}
+
 }  // namespace
 }  // namespace xattn
 
@@ -399,12 +477,13 @@ extern "C" void launch_wmma_kernel(const __half* Q, const __half* K, const __hal
   if (bad_sizes(batch_size, N_latent, N_input, dim)) { set_error(XATTN_ERR_ARG); return; }
   if (batch_size == 0 || N_latent == 0) { set_error(XATTN_OK); return; }
   if (N_input == 0) { set_error(zero_output(output, batch_size, N_latent, dim, stream)); return; }
-  int dev = 0;
-  int rc = prepare_device(&dev);
-  if (rc != XATTN_OK) { set_error(rc); return; }
+  if (Q == nullptr || K == nullptr || V == nullptr || output == nullptr) {
+    set_error(XATTN_ERR_ARG);
+    return;
+  }
   // Q arrives pre-scaled by 1/sqrt(dim) (cuda_wrappers.py:635-640): score scale is 1.
-  set_error(launch_simt<__half, float>(Q, K, V, output, nullptr, nullptr, nullptr, batch_size, 1,
-                                       N_latent, N_input, dim, 1, N_input, 0, kLog2e, stream));
+  set_error(run_half(Q, K, V, output, nullptr, nullptr, nullptr, batch_size, N_latent, N_input,
+                     dim, 0, stream));
 }
 
 extern "C" void launch_splitk_kernel(const float* Q, const float* K, const float* V, float* output,
@@ -422,16 +501,13 @@ extern "C" void launch_wmma_splitk_kernel(const __half* Q, const __half* K, cons
     return;
   }
   if (batch_size == 0 || N_latent == 0) { set_error(XATTN_OK); return; }
-  int dev = 0;
-  int rc = prepare_device(&dev);
-  if (rc != XATTN_OK) { set_error(rc); return; }
-  // Chunk rounded up to a multiple of 16 keys (kernel_wmma_splitk.cu:52).
-  const int chunk = std::max(16, ((N_input + num_splits - 1) / num_splits + 15) / 16 * 16);
-  rc = launch_simt<__half, float>(Q, K, V, nullptr, po, pm, pl, batch_size, 1, N_latent, N_input,
-                                  dim, num_splits, chunk, 1, kLog2e, stream);
-  if (rc != XATTN_OK) { set_error(rc); return; }
-  set_error(launch_combine(po, pm, pl, output, static_cast<long long>(batch_size) * N_latent, dim,
-                           num_splits, stream));
+  if (Q == nullptr || K == nullptr || V == nullptr || output == nullptr || po == nullptr ||
+      pm == nullptr || pl == nullptr) {
+    set_error(XATTN_ERR_ARG);
+    return;
+  }
+  set_error(run_half(Q, K, V, output, po, pm, pl, batch_size, N_latent, N_input, dim, num_splits,
+                     stream));
 }
 
 // ===================================================================== Part 2: new API

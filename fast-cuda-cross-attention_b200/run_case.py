@@ -2,12 +2,14 @@
 
     python fast-cuda-cross-attention_b200/run_case.py --batch 16 --n-latent 1024 \
         --n-input 784 --dim 768 --iters 3 [--kernel 0|1|2] [--splits S] [--bf16-heads H]
+        [--fp16]
 
 Inputs are seeded standard-normal fp32 tensors [B, N, D] created on the device; each
 iteration is one call of xattn.cross_attention (the fp32 entry, xattn_fp32).  --kernel
 selects the fused kernel (0 automatic, 1 two-CTA, 2 four-CTA pair) and --splits forces a
 key split count, through xattn_set_option.  --bf16-heads H instead runs the multi-head
-bf16 entry (xattn_bf16_mha) with H heads of dim / H columns on bf16 inputs.  Prints the
+bf16 entry (xattn_bf16_mha) with H heads of dim / H columns on bf16 inputs; --fp16 runs the
+upstream fp16 entry (launch_wmma_kernel) with Q pre-scaled by 1/sqrt(dim).  Prints the
 mean time per call from CUDA events (not meaningful under a profiler) and checks the last
 output against a float64 reference on the first batch.
 """
@@ -30,6 +32,7 @@ def main():
     ap.add_argument("--kernel", type=int, default=0)
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--bf16-heads", type=int, default=0)
+    ap.add_argument("--fp16", action="store_true")
     a = ap.parse_args()
 
     import torch
@@ -46,10 +49,23 @@ def main():
     if h:
         q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
 
+    if a.fp16:
+        import ctypes
+
+        q, k, v = (q / math.sqrt(a.dim)).half(), k.half(), v.half()
+        o16 = torch.empty(q.shape, device="cuda", dtype=torch.float32)
+        lib = xattn.lib()
+        lib.launch_wmma_kernel.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+
     def call():
+        if a.fp16:
+            lib.launch_wmma_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), o16.data_ptr(),
+                                   a.batch, a.n_latent, a.n_input, a.dim, None)
+            return o16
         return xattn.cross_attention_bf16_mha(q, k, v, h) if h else xattn.cross_attention(q, k, v)
 
-    out = call()
+    for _ in range(10):  # warm-up: clocks ramp from idle, first-call setup
+        out = call()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -61,7 +77,8 @@ def main():
     dh = a.dim // h if h else a.dim
     nh = h if h else 1
     q0, k0, v0 = (x[0].double().view(x.shape[1], nh, dh).transpose(0, 1) for x in (q, k, v))
-    ref = (torch.softmax(q0 @ k0.transpose(1, 2) / math.sqrt(dh), -1) @ v0).transpose(0, 1)
+    qscale = 1.0 if a.fp16 else 1.0 / math.sqrt(dh)  # the fp16 entry takes Q pre-scaled
+    ref = (torch.softmax(q0 @ k0.transpose(1, 2) * qscale, -1) @ v0).transpose(0, 1)
     ref = ref.reshape(a.n_latent, a.dim)
     err = (out[0].double() - ref).abs().max().item() / ref.abs().max().item()
     tflops = xattn.flops(a.batch, a.n_latent, a.n_input, a.dim) / (ms * 1e-3) / 1e12

@@ -302,6 +302,48 @@ def test_wmma_fp16_entries(X, torch_cuda):
     assert_close(torch, torch.from_numpy(out2).cuda(), ref, TF32_TOL, "wmma-splitk")
 
 
+FP16_SHAPES = [(2, 64, 784, 768), (16, 1024, 784, 768), (3, 130, 300, 512), (1, 1, 1, 768),
+               (2, 200, 1000, 256), (1, 77, 333, 64)]
+
+
+@pytest.mark.parametrize("shape", FP16_SHAPES)
+@pytest.mark.parametrize("splits", [0, 1, 3, 7])
+def test_fp16_entries_tensor_core(X, torch_cuda, shape, splits):
+    """launch_wmma_kernel (splits = 0) and launch_wmma_splitk_kernel against float64 on the
+    exact fp16 values, Q pre-scaled by 1/sqrt(D) as upstream callers do
+    (cuda_wrappers.py:635-640).  fp16 values are exact in TF32, so the tensor-core path
+    meets the TF32 tolerance with room to spare."""
+    import ctypes
+
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    if splits and b * nl > 4096:
+        pytest.skip("split entry checked on the smaller shapes")
+    gen = torch.Generator(device="cuda").manual_seed(31)
+    q = (torch.randn(b, nl, d, device="cuda", generator=gen) / math.sqrt(d)).half()
+    k, v = (torch.randn(b, ni, d, device="cuda", generator=gen).half() for _ in range(2))
+    out, intact = guarded_empty(torch, (b, nl, d), torch.float32)
+    lib = X.lib()
+    P, I = ctypes.c_void_p, ctypes.c_int
+    if splits == 0:
+        lib.launch_wmma_kernel.argtypes = [P] * 4 + [I] * 4 + [P]
+        lib.launch_wmma_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni, d, None)
+    else:
+        po = torch.empty(b, nl, splits, d, device="cuda")
+        pm = torch.empty(b, nl, splits, device="cuda")
+        pl = torch.empty_like(pm)
+        lib.launch_wmma_splitk_kernel.argtypes = [P] * 7 + [I] * 5 + [P]
+        lib.launch_wmma_splitk_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                                      po.data_ptr(), pm.data_ptr(), pl.data_ptr(), b, nl, ni, d,
+                                      splits, None)
+    torch.cuda.synchronize()
+    assert lib.xattn_last_error() == 0
+    assert intact()
+    exact = torch.softmax(q.double() @ k.double().transpose(1, 2), -1) @ v.double()
+    assert_close(torch, out.double(), exact, TF32_TOL, f"fp16 {shape} S={splits}")
+    assert X.device_status() == 0
+
+
 BF16_SHAPES = [(2, 128, 200, 8, 96), (1, 33, 65, 4, 64), (32, 1024, 784, 8, 96),
                (3, 257, 1, 2, 128), (1, 130, 129, 3, 96), (2, 64, 1000, 1, 64), (1, 5, 70, 8, 32)]
 
