@@ -102,10 +102,13 @@ struct __align__(8) Barriers {
   uint64_t drain;    // MMA issuer: everything it issued has completed
 };
 
+// Round a non-negative finite fp32 value to TF32 (10 explicit mantissa bits), to nearest with
+// ties away from zero: add half the weight of the 13 dropped bits, then clear them (a carry
+// into the exponent is the correctly rounded result).  Equal to cvt.rna.tf32.f32 for the
+// softmax weights it is used on (0 <= P <= 2^8), but runs on the integer pipe instead of
+// the conversion unit, which the exponentials already keep busy.
 __device__ __forceinline__ uint32_t f2tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+  return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 
 // Exchange layout of the received partial scores, chunk-major: 16-byte chunk i (keys
