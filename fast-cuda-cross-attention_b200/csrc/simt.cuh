@@ -108,33 +108,74 @@ __global__ void __launch_bounds__(kWarps * 32) attention_kernel(const Args<Tin, 
 
 // Log-sum-exp merge of S split partials per row (upstream kernel_splitk.cu:186-236):
 // M = max_s m_s; L = sum_s e^(m_s-M) l_s; O = sum_s e^(m_s-M) O_s / L.  Splits whose
-// m is -FLT_MAX (empty) are skipped.  One warp per row, any D.
+// m is -FLT_MAX (empty) are skipped.  Block (row, column slice) of kCombineThreads threads:
+// warp 0 reduces the row's split weights w_s = e^(m_s-M) / L into shared memory once, then
+// each thread merges four columns at a time with independent loads across the splits.
+// Dynamic shared memory: num_splits floats.
+constexpr int kCombineThreads = 128;
+constexpr int kCombineCols = 4 * kCombineThreads;  // columns per block (float4 per thread)
+
 template <typename Tout>
-__global__ void __launch_bounds__(128) combine_kernel(const float* __restrict__ po,
-                                                      const float* __restrict__ pm,
-                                                      const float* __restrict__ pl,
-                                                      Tout* __restrict__ out, long long rows,
-                                                      int dim, int num_splits, int ld_o) {
-  const long long r = static_cast<long long>(blockIdx.x) * 4 + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ po,
+                                                                  const float* __restrict__ pm,
+                                                                  const float* __restrict__ pl,
+                                                                  Tout* __restrict__ out,
+                                                                  long long rows, int dim,
+                                                                  int num_splits, int ld_o) {
+  extern __shared__ float w[];
+  const long long r = blockIdx.x;
   if (r >= rows) return;
   const float* m = pm + r * num_splits;
   const float* l = pl + r * num_splits;
-  float mx = -INFINITY;
-  for (int s = 0; s < num_splits; ++s)
-    if (m[s] > -3.4028234663852886e38f) mx = fmaxf(mx, m[s]);
-  float lsum = 0.f;
-  for (int s = 0; s < num_splits; ++s)
-    if (m[s] > -3.4028234663852886e38f) lsum += __expf(m[s] - mx) * l[s];
-  const float inv = 1.f / lsum;
-  Tout* dst = out + r * static_cast<long long>(ld_o);
-  for (int d = lane; d < dim; d += 32) {
-    float acc = 0.f;
-    for (int s = 0; s < num_splits; ++s) {
-      if (!(m[s] > -3.4028234663852886e38f)) continue;
-      acc = fmaf(__expf(m[s] - mx), po[(r * num_splits + s) * dim + d], acc);
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    float mx = -INFINITY;
+    for (int s = lane; s < num_splits; s += 32)
+      if (m[s] > -3.4028234663852886e38f) mx = fmaxf(mx, m[s]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float lsum = 0.f;
+    for (int s = lane; s < num_splits; s += 32) {
+      const float e = m[s] > -3.4028234663852886e38f ? __expf(m[s] - mx) : 0.f;
+      w[s] = e;
+      lsum += e * l[s];
     }
-    from_f(&dst[d], acc * inv);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;  // a row with no keys merges to zeros
+    __syncwarp();
+    for (int s = lane; s < num_splits; s += 32) w[s] *= inv;
+  }
+  __syncthreads();
+  const float* src = po + r * num_splits * static_cast<long long>(dim);
+  Tout* dst = out + r * static_cast<long long>(ld_o);
+  const int c0 = blockIdx.y * kCombineCols + 4 * threadIdx.x;
+  // float4 loads need a 16-byte aligned row start: dim % 4 == 0 and an aligned po (caller
+  // scratch of the upstream split entry may be any float pointer)
+  if ((dim & 3) == 0 && (reinterpret_cast<uintptr_t>(po) & 15) == 0) {
+    if (c0 >= dim) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s = 0; s < num_splits; ++s) {
+      const float ws = w[s];
+      if (ws == 0.f) continue;
+      const float4 x = *reinterpret_cast<const float4*>(src + static_cast<long long>(s) * dim + c0);
+      acc.x = fmaf(ws, x.x, acc.x);
+      acc.y = fmaf(ws, x.y, acc.y);
+      acc.z = fmaf(ws, x.z, acc.z);
+      acc.w = fmaf(ws, x.w, acc.w);
+    }
+    from_f(&dst[c0], acc.x);
+    from_f(&dst[c0 + 1], acc.y);
+    from_f(&dst[c0 + 2], acc.z);
+    from_f(&dst[c0 + 3], acc.w);
+  } else {
+    for (int c = c0; c < min(c0 + 4, dim); ++c) {
+      float acc = 0.f;
+      for (int s = 0; s < num_splits; ++s)
+        if (w[s] != 0.f) acc = fmaf(w[s], src[static_cast<long long>(s) * dim + c], acc);
+      from_f(&dst[c], acc);
+    }
   }
 }
 

@@ -272,9 +272,16 @@ int launch_simt(const Tin* Q, const Tin* K, const Tin* V, Tout* out, float* po, 
 int launch_combine(const float* po, const float* pm, const float* pl, float* out, long long rows,
                    int D, int num_splits, cudaStream_t stream) {
   if (rows <= 0) return XATTN_OK;
-  const long long blocks = (rows + 3) / 4;
-  simt::combine_kernel<float><<<static_cast<unsigned>(blocks), 128, 0, stream>>>(
-      po, pm, pl, out, rows, D, num_splits, D);
+  if (rows > 0x7fffffffLL || num_splits <= 0) return XATTN_ERR_ARG;
+  const size_t smem = static_cast<size_t>(num_splits) * sizeof(float);
+  if (smem > 227 * 1024) return XATTN_ERR_ARG;
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(simt::combine_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(smem)) != cudaSuccess)
+    return XATTN_ERR_LAUNCH;
+  const dim3 grid(static_cast<unsigned>(rows), (D + simt::kCombineCols - 1) / simt::kCombineCols);
+  simt::combine_kernel<float><<<grid, simt::kCombineThreads, smem, stream>>>(po, pm, pl, out, rows,
+                                                                             D, num_splits, D);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 

@@ -2,14 +2,15 @@
 
     python fast-cuda-cross-attention_b200/run_case.py --batch 16 --n-latent 1024 \
         --n-input 784 --dim 768 --iters 3 [--kernel 0|1|2] [--splits S] [--bf16-heads H]
-        [--fp16]
+        [--fp16] [--kv-std 0.5]
 
 Inputs are seeded standard-normal fp32 tensors [B, N, D] created on the device; each
 iteration is one call of xattn.cross_attention (the fp32 entry, xattn_fp32).  --kernel
 selects the fused kernel (0 automatic, 1 two-CTA, 2 four-CTA pair) and --splits forces a
 key split count, through xattn_set_option.  --bf16-heads H instead runs the multi-head
 bf16 entry (xattn_bf16_mha) with H heads of dim / H columns on bf16 inputs; --fp16 runs the
-upstream fp16 entry (launch_wmma_kernel) with Q pre-scaled by 1/sqrt(dim).  Prints the
+upstream fp16 entry (launch_wmma_kernel) with Q pre-scaled by 1/sqrt(dim); --kv-std scales
+K and V (config 4 draws them from N(0, 0.5^2)).  Prints the
 mean time per call from CUDA events (not meaningful under a profiler) and checks the last
 output against a float64 reference on the first batch.
 """
@@ -33,6 +34,7 @@ def main():
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--bf16-heads", type=int, default=0)
     ap.add_argument("--fp16", action="store_true")
+    ap.add_argument("--kv-std", type=float, default=1.0)
     a = ap.parse_args()
 
     import torch
@@ -45,6 +47,8 @@ def main():
     q = torch.randn(a.batch, a.n_latent, a.dim, device="cuda", generator=gen)
     k = torch.randn(a.batch, a.n_input, a.dim, device="cuda", generator=gen)
     v = torch.randn(a.batch, a.n_input, a.dim, device="cuda", generator=gen)
+    if a.kv_std != 1.0:
+        k, v = k * a.kv_std, v * a.kv_std
     h = a.bf16_heads
     if h:
         q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()

@@ -302,6 +302,28 @@ def test_wmma_fp16_entries(X, torch_cuda):
     assert_close(torch, torch.from_numpy(out2).cuda(), ref, TF32_TOL, "wmma-splitk")
 
 
+def test_config4_long_input_full_size(X, torch_cuda):
+    """Config 4 at full size: B=8, N_latent=512, N_input=65536, D=768, Q ~ N(0,1), K,V ~
+    N(0, 0.5^2), through the automatic path (key split over the library workspace and the
+    log-sum-exp combine).  Sampled rows of every batch against float64 on the same inputs."""
+    torch = torch_cuda
+    b, nl, ni, d = 8, 512, 65536, 768
+    gen = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn(b, nl, d, device="cuda", generator=gen)
+    k = torch.randn(b, ni, d, device="cuda", generator=gen) * 0.5
+    v = torch.randn(b, ni, d, device="cuda", generator=gen) * 0.5
+    out = X.cross_attention(q, k, v)
+    torch.cuda.synchronize()
+    rows = torch.arange(0, nl, 37, device="cuda")
+    worst = 0.0
+    for i in range(b):
+        qq = q[i, rows].double()
+        ref = torch.softmax(qq @ k[i].double().T / math.sqrt(d), -1) @ v[i].double()
+        worst = max(worst, (out[i, rows].double() - ref).abs().max().item() / ref.abs().max().item())
+    assert worst <= TF32_TOL, f"config 4: {worst:.3e}"
+    assert X.device_status() == 0
+
+
 FP16_SHAPES = [(2, 64, 784, 768), (16, 1024, 784, 768), (3, 130, 300, 512), (1, 1, 1, 768),
                (2, 200, 1000, 256), (1, 77, 333, 64)]
 
