@@ -20,6 +20,7 @@
 #include <tuple>
 #include <utility>
 
+#include "accurate.cuh"
 #include "fused_tf32.cuh"
 #include "fused_tf32_pair.cuh"
 #include "mha_bf16.cuh"
@@ -43,6 +44,7 @@ std::atomic<int> g_opt_splits{0};
 std::atomic<int> g_opt_wait_us{2000000};
 std::atomic<int> g_opt_tf32_comp{1};
 std::atomic<int> g_opt_kernel{0};  // 0 auto, 1 two-CTA kernel, 2 four-CTA pair kernel
+std::atomic<int> g_opt_accurate{0};  // 1: fp32 entries use the 3xTF32 accurate mode
 
 int set_error(int code) {
   t_last_error = code;
@@ -73,6 +75,11 @@ int prepare_device(int* dev_out) {
     if (cudaFuncSetAttribute(pair4::fused_tf32_pair_kernel,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pair4::kSmemBytes) != cudaSuccess)
+      return XATTN_ERR_LAUNCH;
+    if (cudaFuncSetAttribute(accurate::gemm3x_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, accurate::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(accurate::gemm3x_kernel<true>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, accurate::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
     if (cudaFuncSetAttribute(mha::mha_bf16_kernel<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, mha::kSmemBytes) != cudaSuccess ||
@@ -318,6 +325,88 @@ void plan_splits(int dev, int B, int Nl, int Ni, int path, int* splits_out, int*
 }
 
 // The fp32 entry: all four upstream fp32 names and xattn_fp32 land here.
+// ------------------------------------------------------------------ 3xTF32 accurate mode
+// Batched GEMM launch: C[b] = A[b] (m x k, K-major) x B[b]^T (K-major, n x k) or x B[b]
+// (MN-major, k x n).  a_ld / b_ld are row strides in floats; the maps bound rows and K by
+// m, n, k, so the TMA zero-fills beyond them whatever the row padding holds.
+int launch_gemm3x(const float* A, const float* As, int a_ld, const float* Bm, const float* Bs,
+                  int b_ld, bool b_mn_major, float* C, int ldc, int batch, int m, int n, int k,
+                  cudaStream_t stream) {
+  accurate::GemmParams p;
+  const uint64_t da[3] = {(uint64_t)k, (uint64_t)m, (uint64_t)batch};
+  const uint64_t sa[2] = {(uint64_t)a_ld * 4, (uint64_t)m * a_ld * 4};
+  const uint32_t ba[3] = {accurate::kChunk, accurate::kTile, 1};
+  if (!encode_tmap(&p.ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, A, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_tmap(&p.tas, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, As, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B))
+    return XATTN_ERR_ARG;
+  if (b_mn_major) {  // B is k x n, rows contiguous along n: {32 columns, k rows, n/32 slabs, batch}
+    const uint64_t db[4] = {(uint64_t)accurate::kChunk, (uint64_t)k, (uint64_t)n / accurate::kChunk,
+                            (uint64_t)batch};
+    const uint64_t sb[3] = {(uint64_t)b_ld * 4, (uint64_t)accurate::kChunk * 4, (uint64_t)k * b_ld * 4};
+    const uint32_t bb[4] = {accurate::kChunk, accurate::kChunk, accurate::kTile / accurate::kChunk, 1};
+    if (!encode_tmap(&p.tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Bm, db, sb, bb,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+        !encode_tmap(&p.tbs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, Bs, db, sb, bb,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+      return XATTN_ERR_ARG;
+  } else {
+    const uint64_t db[3] = {(uint64_t)k, (uint64_t)n, (uint64_t)batch};
+    const uint64_t sb[2] = {(uint64_t)b_ld * 4, (uint64_t)n * b_ld * 4};
+    if (!encode_tmap(&p.tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, Bm, db, sb, ba, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&p.tbs, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, Bs, db, sb, ba, CU_TENSOR_MAP_SWIZZLE_128B))
+      return XATTN_ERR_ARG;
+  }
+  p.c = C;
+  p.c_batch_stride = static_cast<long long>(m) * ldc;
+  p.ldc = ldc;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.tiles_m = (m + accurate::kTile - 1) / accurate::kTile;
+  p.tiles_n = (n + accurate::kTile - 1) / accurate::kTile;
+  const long long ctas = static_cast<long long>(p.tiles_m) * p.tiles_n * batch;
+  if (ctas > 0x7fffffffLL) return XATTN_ERR_ARG;
+  if (b_mn_major)
+    accurate::gemm3x_kernel<true><<<static_cast<unsigned>(ctas), accurate::kThreads,
+                                    accurate::kSmemBytes, stream>>>(p);
+  else
+    accurate::gemm3x_kernel<false><<<static_cast<unsigned>(ctas), accurate::kThreads,
+                                     accurate::kSmemBytes, stream>>>(p);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+// fp32 attention in the 3xTF32 accurate mode (accurate.cuh): residuals of Q, K, V; S = Q K^T;
+// row softmax into P (+ residual); O = P V.  Workspace: 2 B Nl Ni_pad + B Nl D + 2 B Ni D
+// floats (Ni_pad = Ni rounded up to 4, a 16-byte row stride).
+int run_fp32_accurate(int dev, const float* Q, const float* K, const float* V, float* O, int B,
+                      int Nl, int Ni, int D, cudaStream_t stream) {
+  const int ni_pad = (Ni + 3) / 4 * 4;
+  const size_t nq = static_cast<size_t>(B) * Nl * D, nk = static_cast<size_t>(B) * Ni * D;
+  const size_t ns = static_cast<size_t>(B) * Nl * ni_pad;
+  auto r64 = [](size_t n) { return (n + 63) / 64 * 64; };
+  float* ws = static_cast<float*>(
+      workspace(dev, stream, (r64(nq) + 2 * r64(nk) + 2 * r64(ns)) * sizeof(float)));
+  if (ws == nullptr) return XATTN_ERR_NOMEM;
+  float* qs = ws;
+  float* ks = qs + r64(nq);
+  float* vs = ks + r64(nk);
+  float* sp = vs + r64(nk);   // S, then P in place
+  float* ps = sp + r64(ns);   // residual of P
+  const int sms = sm_count(dev);
+  for (auto [src, dst, n] : {std::tuple<const float*, float*, size_t>{Q, qs, nq}, {K, ks, nk}, {V, vs, nk}}) {
+    const unsigned blocks = static_cast<unsigned>(std::min<long long>((n + 255) / 256, sms * 8LL));
+    accurate::split_residual_kernel<<<blocks, 256, 0, stream>>>(src, dst, static_cast<long long>(n));
+  }
+  if (cudaPeekAtLastError() != cudaSuccess) return XATTN_ERR_LAUNCH;
+  int rc = launch_gemm3x(Q, qs, D, K, ks, D, false, sp, ni_pad, B, Nl, Ni, D, stream);
+  if (rc != XATTN_OK) return rc;
+  const long long rows = static_cast<long long>(B) * Nl;
+  accurate::softmax_rows_kernel<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, stream>>>(
+      sp, ps, rows, Ni, ni_pad, static_cast<float>(1.0 / std::sqrt(static_cast<double>(D))));
+  if (cudaPeekAtLastError() != cudaSuccess) return XATTN_ERR_LAUNCH;
+  return launch_gemm3x(sp, ps, ni_pad, V, vs, D, true, O, D, B, Nl, D, Ni, stream);
+}
+
 int run_fp32(const float* Q, const float* K, const float* V, float* O, int B, int Nl, int Ni,
              int D, cudaStream_t stream) {
   if (bad_sizes(B, Nl, Ni, D)) return set_error(XATTN_ERR_ARG);
@@ -330,6 +419,15 @@ int run_fp32(const float* Q, const float* K, const float* V, float* O, int B, in
   if (rc != XATTN_OK) return set_error(rc);
   const int path = g_opt_path.load();
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(D));
+  if (g_opt_accurate.load() != 0 && path != 2) {
+    // 3xTF32 on the tensor cores where TMA can read the operands; otherwise the generic
+    // kernel, which computes in plain fp32 and is as accurate
+    if (D % 32 == 0 && aligned16(Q) && aligned16(K) && aligned16(V) && aligned16(O) &&
+        static_cast<long long>(B) * Nl < 0x7fffffffLL)
+      return set_error(run_fp32_accurate(dev, Q, K, V, O, B, Nl, Ni, D, stream));
+    return set_error(launch_simt<float, float>(Q, K, V, O, nullptr, nullptr, nullptr, B, 1, Nl, Ni,
+                                               D, 1, Ni, 0, scale_log2, stream));
+  }
   if (path == 2 || !tc_fp32_supported(Q, K, V, O, D)) {
     return set_error(launch_simt<float, float>(Q, K, V, O, nullptr, nullptr, nullptr, B, 1, Nl, Ni,
                                                D, 1, Ni, 0, scale_log2, stream));
@@ -668,6 +766,7 @@ extern "C" int xattn_set_option(int key, int value) {
     case 3: return g_opt_wait_us.exchange(value > 0 ? value : 2000000);
     case 4: return g_opt_tf32_comp.exchange(value);
     case 5: return g_opt_kernel.exchange(value);
+    case 6: return g_opt_accurate.exchange(value);
     default: return -1;
   }
 }

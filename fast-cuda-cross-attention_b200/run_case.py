@@ -2,7 +2,7 @@
 
     python fast-cuda-cross-attention_b200/run_case.py --batch 16 --n-latent 1024 \
         --n-input 784 --dim 768 --iters 3 [--kernel 0|1|2] [--splits S] [--bf16-heads H]
-        [--fp16] [--kv-std 0.5]
+        [--fp16] [--kv-std 0.5] [--accurate]
 
 Inputs are seeded standard-normal fp32 tensors [B, N, D] created on the device; each
 iteration is one call of xattn.cross_attention (the fp32 entry, xattn_fp32).  --kernel
@@ -10,7 +10,8 @@ selects the fused kernel (0 automatic, 1 two-CTA, 2 four-CTA pair) and --splits 
 key split count, through xattn_set_option.  --bf16-heads H instead runs the multi-head
 bf16 entry (xattn_bf16_mha) with H heads of dim / H columns on bf16 inputs; --fp16 runs the
 upstream fp16 entry (launch_wmma_kernel) with Q pre-scaled by 1/sqrt(dim); --kv-std scales
-K and V (config 4 draws them from N(0, 0.5^2)).  Prints the
+K and V (config 4 draws them from N(0, 0.5^2)); --accurate selects the 3xTF32 mode of the
+fp32 entry (option 6).  Prints the
 mean time per call from CUDA events (not meaningful under a profiler) and checks the last
 output against a float64 reference on the first batch.
 """
@@ -35,6 +36,7 @@ def main():
     ap.add_argument("--bf16-heads", type=int, default=0)
     ap.add_argument("--fp16", action="store_true")
     ap.add_argument("--kv-std", type=float, default=1.0)
+    ap.add_argument("--accurate", action="store_true")
     a = ap.parse_args()
 
     import torch
@@ -43,6 +45,7 @@ def main():
 
     xattn.set_option(xattn.OPT_KERNEL, a.kernel)
     xattn.set_option(xattn.OPT_SPLITS, a.splits)
+    xattn.set_option(6, 1 if a.accurate else 0)
     gen = torch.Generator(device="cuda").manual_seed(1234)
     q = torch.randn(a.batch, a.n_latent, a.dim, device="cuda", generator=gen)
     k = torch.randn(a.batch, a.n_input, a.dim, device="cuda", generator=gen)
@@ -88,7 +91,7 @@ def main():
     tflops = xattn.flops(a.batch, a.n_latent, a.n_input, a.dim) / (ms * 1e-3) / 1e12
     print(f"B={a.batch} Nl={a.n_latent} Ni={a.n_input} D={a.dim}: {ms * 1e3:.1f} us/call "
           f"{tflops:.1f} TFLOP/s  rel err {err:.2e}  status {xattn.device_status()}")
-    if not err < (2e-2 if h else 2e-3) or xattn.device_status() != 0:
+    if not err < (2e-2 if h else (1e-5 if a.accurate else 2e-3)) or xattn.device_status() != 0:
         sys.exit(1)
 
 

@@ -46,7 +46,7 @@ EXPORTED = (
     "xattn_version", "xattn_plan_fp32", "xattn_splitk_noalloc",
 )
 
-OPT_PATH, OPT_SPLITS, OPT_WAIT_US, OPT_TF32_COMP, OPT_KERNEL = 1, 2, 3, 4, 5
+OPT_PATH, OPT_SPLITS, OPT_WAIT_US, OPT_TF32_COMP, OPT_KERNEL, OPT_ACCURATE = 1, 2, 3, 4, 5, 6
 
 
 def lib():

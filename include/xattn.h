@@ -171,8 +171,11 @@ int xattn_status(int clear);
  * tensor-core fp32 path: 1 (default) scales scores by (1 + 2e) and the output by (1 + e),
  * e = 2^-11 / (2 ln 2), the mean relative truncation error of one operand; 0 turns it
  * off (for inputs already exact in TF32).  key 5 = fp32 tensor-core kernel: 0 auto, 1 the
- * two-CTA kernel, 2 the four-CTA pair kernel (where the shape allows it).  Returns the
- * previous value.                                                                       */
+ * two-CTA kernel, 2 the four-CTA pair kernel (where the shape allows it).  key 6 = accurate
+ * fp32 mode: 1 makes the non-split fp32 entries compute with 3xTF32 on the tensor cores
+ * (two 3xTF32 GEMMs around an exact row softmax; max|dO| <= 1e-5 * max|O|; workspace of
+ * 2 B N_latent N_input + B N_latent D + 2 B N_input D floats), 0 (default) the fused TF32
+ * kernels.  Returns the previous value.                                                 */
 int xattn_set_option(int key, int value);
 
 /* Runs a kernel that waits on an mbarrier nothing will ever arrive on, with the wait

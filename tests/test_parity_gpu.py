@@ -324,6 +324,53 @@ def test_config4_long_input_full_size(X, torch_cuda):
     assert X.device_status() == 0
 
 
+ACCURATE_SHAPES = [(1, 64, 784, 768), (2, 130, 781, 768), (3, 257, 300, 512), (1, 1, 1, 768),
+                   (2, 100, 1000, 320), (4, 1024, 784, 768)]
+
+
+@pytest.mark.parametrize("shape", ACCURATE_SHAPES)
+def test_accurate_3xtf32_mode(X, torch_cuda, shape):
+    """Option 6 = 1: the 3xTF32 mode (two 3xTF32 tensor-core GEMMs around an exact row
+    softmax) meets the north-star bound max|dO| <= 1e-5 * max|O_ref| against float64, on
+    ragged N_input (padded row stride), tail tiles in M and N, and the single-key case."""
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    gen = torch.Generator(device="cuda").manual_seed(41)
+    q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+    X.set_option(6, 1)
+    try:
+        out, intact = guarded_empty(torch, (b, nl, d), torch.float32)
+        X.cross_attention(q, k, v, out=out)
+        torch.cuda.synchronize()
+    finally:
+        X.set_option(6, 0)
+    assert intact()
+    exact = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(d), -1) @ v.double()
+    assert_close(torch, out.double(), exact, 1e-5, f"3xTF32 {shape}")
+    assert X.device_status() == 0
+
+
+def test_accurate_mode_through_upstream_entry(X, torch_cuda):
+    import ctypes
+
+    torch = torch_cuda
+    b, nl, ni, d = 2, 64, 784, 768
+    gen = torch.Generator(device="cuda").manual_seed(42)
+    q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+    out = torch.empty_like(q)
+    lib = X.lib()
+    lib.launch_optimized_kernel.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    X.set_option(6, 1)
+    try:
+        lib.launch_optimized_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni, d, None)
+        torch.cuda.synchronize()
+    finally:
+        X.set_option(6, 0)
+    assert lib.xattn_last_error() == 0
+    exact = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(d), -1) @ v.double()
+    assert_close(torch, out.double(), exact, 1e-5, "3xTF32 via launch_optimized_kernel")
+
+
 FP16_SHAPES = [(2, 64, 784, 768), (16, 1024, 784, 768), (3, 130, 300, 512), (1, 1, 1, 768),
                (2, 200, 1000, 256), (1, 77, 333, 64)]
 
