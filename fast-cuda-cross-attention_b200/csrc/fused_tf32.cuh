@@ -63,7 +63,14 @@ constexpr int kTmemCols = 512;
 constexpr int kXBytes = kRows * kKeys * 4;  // one exchange / P buffer: a 128x128 fp32 tile
 constexpr int kXBufs = 2;                   // double-buffered across key tiles
 constexpr int kMaxDh = 384;                 // D <= 768
-constexpr int kThreads = 64 + kSoftmaxThreads;
+// Warps: 0 producer, 1 MMA issuer, 2..9 softmax, 10.. further producers (registers are
+// allocated per group of four warps, so twelve warps cost the softmax warps nothing).
+constexpr int kFirstExtraProducer = 2 + kSoftmaxThreads / 32;
+constexpr int kProducers = 3;
+constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (kProducers - 1);
+// A producer waits for the release of stage i - kStages by parity alone; its previous
+// stage, i + kStages - kProducers, already required stage i - kProducers <= i - kStages.
+static_assert(kProducers <= kStages, "parity-only stage waits need kProducers <= kStages");
 constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
 constexpr float kRescaleLog2 = 8.0f;        // lazy-rescale threshold (factor 256)
 // Static shared memory of the kernel (barriers, reduction arrays, slots), kept in the
@@ -186,41 +193,46 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
   // Ring order, identical for producer and MMA issuer:
   //   QK(0), then for j = 0..n-1: [QK(j+1) if any], V(j).
-  if (warp == 0) {
-    // ================================================================ TMA producer
+  if (warp == 0 || warp >= kFirstExtraProducer) {
+    // ================================================================ TMA producers
+    // Stage i of the ring sequence goes to producer i % kProducers and slot i % kStages;
+    // the slot's use count, hence the empty-barrier parity, follows from i.  One issuing
+    // thread sustains only a few million copies per second.
+    const int pid = warp == 0 ? 0 : warp - kFirstExtraProducer + 1;
     if (elect_one() && n_tiles > 0) {
-      int s = 0;
-      uint32_t phase = 0;
       bool ok = true;
+      int i = 0;
+      auto own = [&](uint32_t bytes) -> bool {
+        if (i % kProducers != pid) return false;
+        const int slot = i % kStages;
+        const uint32_t use = static_cast<uint32_t>(i / kStages);
+        if (use > 0 &&
+            !(ok = mbar_wait(smem_u32(&bars.empty[slot]), (use - 1) & 1u, kTimeoutStageFree, abort)))
+          return false;
+        mbar_arrive_expect_tx(smem_u32(&bars.full[slot]), bytes);
+        return true;
+      };
       auto load_qk = [&](int j) {
         const int key0 = k_begin + j * kKeys;
-        XATTN_TRACE_POINT(0, j);
-        for (int c = 0; c < n_qk_chunks && ok; ++c) {
-          if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)))
-            break;
-          const uint32_t st = smem_u32(stages + s * kStageBytes);
-          const uint32_t fb = smem_u32(&bars.full[s]);
-          mbar_arrive_expect_tx(fb, kStageBytes);
+        if (pid == 0) XATTN_TRACE_POINT(0, j);
+        for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
+          if (!own(kStageBytes)) continue;
+          const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
+          const uint32_t fb = smem_u32(&bars.full[i % kStages]);
           tma_load_3d(st, &p.tq, fb, col0 + c * kChunk, row0, b);
           tma_load_3d(st + 16384, &p.tk, fb, col0 + c * kChunk, key0, b);
-          if (++s == kStages) { s = 0; phase ^= 1u; }
         }
       };
       auto load_v = [&](int j) {
         const int key0 = k_begin + j * kKeys;
         const int valid = min(kKeys, k_end - key0);
         const int n_v = (valid + kVKeys - 1) / kVKeys;
-        XATTN_TRACE_POINT(1, j);
-        for (int v = 0; v < n_v && ok; ++v) {
-          if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort)))
-            break;
-          const uint32_t st = smem_u32(stages + s * kStageBytes);
-          const uint32_t fb = smem_u32(&bars.full[s]);
-          mbar_arrive_expect_tx(fb, n_qk_chunks * kVKeys * 128);
-          for (int sl = 0; sl < n_qk_chunks; ++sl)
-            tma_load_3d(st + sl * (kVKeys * 128), &p.tv, fb, col0 + sl * kChunk,
-                        key0 + v * kVKeys, b);
-          if (++s == kStages) { s = 0; phase ^= 1u; }
+        if (pid == 0) XATTN_TRACE_POINT(1, j);
+        for (int v = 0; v < n_v && ok; ++v, ++i) {
+          if (!own(n_qk_chunks * kVKeys * 128)) continue;
+          // all of this CTA's 32-column slabs of kVKeys keys in one box (slab = dim / 32)
+          tma_load_4d(smem_u32(stages + (i % kStages) * kStageBytes), &p.tv,
+                      smem_u32(&bars.full[i % kStages]), 0, key0 + v * kVKeys, col0 / kChunk, b);
         }
       };
       load_qk(0);
@@ -228,10 +240,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (j + 1 < n_tiles) load_qk(j + 1);
         load_v(j);
       }
-      // Drain: every load issued must land before this CTA may exit.
-      for (int i = 0; i < kStages; ++i) {
-        if (--s < 0) { s = kStages - 1; phase ^= 1u; }
-        mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutDrain, nullptr);
+      // Drain (producer 0): every load issued must land before this CTA may exit.
+      if (pid == 0) {
+        for (int k = max(0, i - kStages); k < i; ++k)
+          mbar_wait(smem_u32(&bars.full[k % kStages]), static_cast<uint32_t>(k / kStages) & 1u,
+                    kTimeoutDrain, nullptr);
       }
     }
   } else if (warp == 1) {

@@ -168,6 +168,17 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
                  bool exact_inputs = false) {
   fused::Params p;
   if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D)) return XATTN_ERR_ARG;
+  {
+    // V as [B][D/32 slabs][Ni keys][32 columns]: one box holds all D/2/32 slabs of a CTA's
+    // half for kVKeys keys, so a V stage is one copy
+    const uint64_t dv[4] = {(uint64_t)fused::kChunk, (uint64_t)Ni, (uint64_t)D / fused::kChunk,
+                            (uint64_t)B};
+    const uint64_t sv[3] = {(uint64_t)D * 4, (uint64_t)fused::kChunk * 4, (uint64_t)Ni * D * 4};
+    const uint32_t bv[4] = {fused::kChunk, fused::kVKeys, (uint32_t)(D / 2 / fused::kChunk), 1};
+    if (!encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, V, dv, sv, bv,
+                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+      return XATTN_ERR_ARG;
+  }
   p.out = out;
   p.po = po;
   p.pm = pm;
