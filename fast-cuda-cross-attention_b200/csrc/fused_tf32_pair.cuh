@@ -184,12 +184,23 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         const int valid = min(kKeys, k_end - key0);
         const int n_qk = (valid + 15) & ~15;
         const int kbase = key0 + static_cast<int>(r) * (n_qk / 2);  // this CTA's half of the keys
-        if (pid == 0) XATTN_TRACE_POINT(0, j);
+        if (pid == 0) {
+          XATTN_TRACE_POINT(0, j);
+          // warm L2 with this tile's V, loaded about one tile from now (a quarter of the
+          // operand reads otherwise miss the near L2 partition)
+          for (int v = 0; v * kVKeys < valid; ++v)
+            for (int n = 0; n < n_instr; ++n)
+              tma_prefetch_4d(&p.tv, 0, key0 + v * kVKeys,
+                              (col0 + n * nn + static_cast<int>(r) * (nn / 2)) / kChunk, b);
+        }
         for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
           if (!own(16384 + 8192)) continue;
           const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
           tma_load_3d_pair(st, &p.tq, fb, col0 + c * kChunk, row0, b);
           tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * kChunk, kbase, b);
+          // and the same chunk of the next tile's keys (out-of-range boxes prefetch nothing)
+          if (j + 1 < n_tiles)
+            tma_prefetch_3d(&p.tk, col0 + c * kChunk, key0 + kKeys + static_cast<int>(r) * (kKeys / 2), b);
         }
       };
       auto load_v = [&](int j) {

@@ -264,6 +264,19 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
+// L2 prefetch of a tensor-map box (no shared memory, no barrier): warms L2 for a copy issued
+// later, so that copy waits on an L2 hit instead of DRAM.
+__device__ __forceinline__ void tma_prefetch_3d(const void* tmap, int x, int y, int z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_4d(const void* tmap, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(tmap),
+               "r"(x), "r"(y), "r"(z), "r"(w)
+               : "memory");
+}
+
 // Four-dimensional form of tma_load_3d_pair (a box of several 32-column slabs in one copy).
 __device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster,
                                                  int x, int y, int z, int w) {
