@@ -111,17 +111,21 @@ __global__ void __launch_bounds__(kWarps * 32) attention_kernel(const Args<Tin, 
 // m is -FLT_MAX (empty) are skipped.  Block (row, column slice) of kCombineThreads threads:
 // warp 0 reduces the row's split weights w_s = e^(m_s-M) / L into shared memory once, then
 // each thread merges four columns at a time with independent loads across the splits.
-// Dynamic shared memory: num_splits floats.
+// Dynamic shared memory: num_splits floats.  kPartial: write the merged partial instead of
+// the normalised output -- O_u = sum_s e^(m_s-M) O_s (unnormalised) to out, M to pm_out and
+// L to pl_out (a row with no keys keeps the empty-split triple -FLT_MAX, 0, 0).
 constexpr int kCombineThreads = 128;
 constexpr int kCombineCols = 4 * kCombineThreads;  // columns per block (float4 per thread)
 
-template <typename Tout>
+template <typename Tout, bool kPartial = false>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ po,
                                                                   const float* __restrict__ pm,
                                                                   const float* __restrict__ pl,
                                                                   Tout* __restrict__ out,
                                                                   long long rows, int dim,
-                                                                  int num_splits, int ld_o) {
+                                                                  int num_splits, int ld_o,
+                                                                  float* __restrict__ pm_out = nullptr,
+                                                                  float* __restrict__ pl_out = nullptr) {
   extern __shared__ float w[];
   const long long r = blockIdx.x;
   if (r >= rows) return;
@@ -142,7 +146,11 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;  // a row with no keys merges to zeros
+    const float inv = kPartial ? 1.f : (lsum > 0.f ? 1.f / lsum : 0.f);  // no keys: zeros
+    if (kPartial && lane == 0 && blockIdx.y == 0) {
+      pm_out[r] = lsum > 0.f ? mx : -3.4028234663852886e38f;
+      pl_out[r] = lsum;
+    }
     __syncwarp();
     for (int s = lane; s < num_splits; s += 32) w[s] *= inv;
   }

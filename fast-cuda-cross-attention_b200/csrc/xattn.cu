@@ -287,19 +287,22 @@ int launch_simt(const Tin* Q, const Tin* K, const Tin* V, Tout* out, float* po, 
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 
+// pm_out / pl_out non-null: write the merged partial (unnormalised O, M, L) instead.
 int launch_combine(const float* po, const float* pm, const float* pl, float* out, long long rows,
-                   int D, int num_splits, cudaStream_t stream) {
+                   int D, int num_splits, cudaStream_t stream, float* pm_out = nullptr,
+                   float* pl_out = nullptr) {
   if (rows <= 0) return XATTN_OK;
   if (rows > 0x7fffffffLL || num_splits <= 0) return XATTN_ERR_ARG;
   const size_t smem = static_cast<size_t>(num_splits) * sizeof(float);
   if (smem > 227 * 1024) return XATTN_ERR_ARG;
+  auto kern = pm_out != nullptr ? simt::combine_kernel<float, true> : simt::combine_kernel<float, false>;
   if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(simt::combine_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return XATTN_ERR_LAUNCH;
   const dim3 grid(static_cast<unsigned>(rows), (D + simt::kCombineCols - 1) / simt::kCombineCols);
-  simt::combine_kernel<float><<<grid, simt::kCombineThreads, smem, stream>>>(po, pm, pl, out, rows,
-                                                                             D, num_splits, D);
+  kern<<<grid, simt::kCombineThreads, smem, stream>>>(po, pm, pl, out, rows, D, num_splits, D, pm_out,
+                                                      pl_out);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 
@@ -642,12 +645,30 @@ extern "C" int xattn_fp32_partial(const float* Q, const float* K, const float* V
   int rc = prepare_device(&dev);
   if (rc != XATTN_OK) return set_error(rc);
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(dim));
-  const int chunk = std::max(1, N_input);
-  if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, po, dim))
+  const int path = g_opt_path.load();
+  if (path == 2 || !tc_fp32_supported(Q, K, V, po, dim))
     return set_error(launch_simt<float, float>(Q, K, V, nullptr, po, pm, pl, batch_size, 1, N_latent,
-                                               N_input, dim, 1, chunk, 1, scale_log2, stream));
-  return set_error(launch_fused(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim, 1,
-                                chunk, 1, stream));
+                                               N_input, dim, 1, std::max(1, N_input), 1,
+                                               scale_log2, stream));
+  // Key splits when the row blocks alone cannot fill the GPU, as for the plain entry; the
+  // splits' partials are then merged into the one (m, l, O) triple asked for.
+  int splits = 1, chunk = std::max(1, N_input);
+  if (N_input > 0) plan_splits(dev, batch_size, N_latent, N_input, path, &splits, &chunk);
+  if (splits == 1)
+    return set_error(launch_fused(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim,
+                                  1, std::max(1, N_input), 1, stream));
+  const size_t rows = static_cast<size_t>(batch_size) * N_latent;
+  const size_t po_elems = rows * splits * dim, ml_elems = rows * splits;
+  float* ws = static_cast<float*>(workspace(dev, stream, (po_elems + 2 * ml_elems + 64) * sizeof(float)));
+  if (ws == nullptr) return set_error(XATTN_ERR_NOMEM);
+  float* wpo = ws;
+  float* wpm = wpo + po_elems;
+  float* wpl = wpm + ml_elems;
+  rc = launch_fused(Q, K, V, nullptr, wpo, wpm, wpl, batch_size, N_latent, N_input, dim, splits,
+                    chunk, 1, stream);
+  if (rc != XATTN_OK) return set_error(rc);
+  return set_error(launch_combine(wpo, wpm, wpl, po, static_cast<long long>(rows), dim, splits,
+                                  stream, pm, pl));
 }
 
 extern "C" int xattn_combine(const float* po, const float* pm, const float* pl, float* output,
