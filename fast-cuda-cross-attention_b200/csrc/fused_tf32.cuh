@@ -345,23 +345,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int key0 = k_begin + j * kKeys;
       const int valid = min(kKeys, k_end - key0);
       // ---- copy S_h out of tensor memory, release the columns to the next Q.K^T
-      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort))) break;
+      // After a failed bounded wait a warp keeps iterating with the work skipped (later waits
+      // fail at once through the abort flag), so every softmax warp reaches each named
+      // barrier equally often and none is left in bar.sync.
+      const int xb_i = j & 1;
+      uint8_t* xcur = xbuf + xb_i * kXBytes;
+      const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
+      const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
+      ok = ok && warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort);
+      uint32_t ra[32], rb[32];
+      float gmax = -INFINITY;
+      if (ok) {
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(6, j);
       tc_fence_after();
-      uint32_t ra[32], rb[32];
       tmem_ld32(t_row + kSCol + cbase, ra);
       tmem_ld32(t_row + kSCol + cbase + 32, rb);
       tmem_ld_wait();
       tc_fence_before();
       mbar_arrive(smem_u32(&bars.s_free));
       // ---- send S_h into the peer's buffer (j % 2) once the peer has released it
-      const int xb_i = j & 1;
-      uint8_t* xcur = xbuf + xb_i * kXBytes;
-      const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
-      const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
-      if (j >= kXBufs && !(ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), j & 1,
-                                                      kTimeoutExchange, abort)))
-        break;
+      if (j >= kXBufs) ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), j & 1,
+                                                      kTimeoutExchange, abort);
+      if (ok) {
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
@@ -375,12 +380,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
       if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[xb_i]), kXBytes);
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
-      if (!(ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), (j >> 1) & 1, kTimeoutPeer,
-                                       abort)))
-        break;
+      ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), (j >> 1) & 1, kTimeoutPeer,
+                                       abort);
+      }
+      if (ok) {
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
       // ---- full score = own + peer, in log2 units, masked; group row max
-      float gmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(ch0 + i, row));
@@ -394,6 +399,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           rv = __float_as_uint(t);
         }
       }
+      }
+      }
       red[grp][row] = gmax;
       // every received score is read before P overwrites the buffer in another layout
       named_bar_sync(1, kSoftmaxThreads);
@@ -403,6 +410,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       for (int g = 1; g < kGroups; ++g) tmax = fmaxf(tmax, red[g][row]);
       // the row maxima are read by both groups before either writes the next tile's
       named_bar_sync(2 + quad, 32 * kGroups);
+      if (!ok) continue;
       m_true = fmaxf(m_true, tmax);
       float alpha = 1.f;
       if (j == 0) {
@@ -415,7 +423,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
         if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
                                   kTimeoutMmaDone, abort)))
-          break;
+          continue;
         tc_fence_after();
         for (int c = grp; c < dh / 32; c += kGroups) {
           uint32_t o[32];
@@ -452,7 +460,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (j >= 1 && j + 1 < n_tiles) {
         if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
                                   kTimeoutMmaDone, abort)))
-          break;
+          continue;
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
         if (lane == 0) mbar_arrive_remote(peer_x_empty);
       }

@@ -329,62 +329,68 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     for (int j = 0; j < n_tiles; ++j) {
       const int key0 = k_begin + j * kKeys;
       const int valid = min(kKeys, k_end - key0);
-      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort))) break;
-      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(6, j);
-      tc_fence_after();
-      uint32_t ra[32], rb[32];
-      tmem_ld32(t_row + kSCol + cbase, ra);
-      tmem_ld32(t_row + kSCol + cbase + 32, rb);
-      tmem_ld_wait();
-      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(18, j);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(lead_s_free);
-      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
       // buffer of tile j: j % kXBufs, used for the (j / kXBufs)-th time
       const int xb_i = j % kXBufs;
       const uint32_t xb_par = static_cast<uint32_t>(j / kXBufs) & 1u;
-      if (kXBufs == 1 && j >= 1) {
-        // single buffer: it held P of tile j-1; free once that P.V completed
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[0]), (j - 1) & 1, kTimeoutMmaDone, abort)))
-          break;
-        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
-        if (lane == 0) mbar_arrive_remote(peer_x_empty);
-      }
       uint8_t* xcur = xbuf + xb_i * kXBytes;
       const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
       const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
-      if (j >= kXBufs && !(ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (j - kXBufs) & 1,
-                                                      kTimeoutExchange, abort)))
-        break;
-      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        st_async_v4(peer_x_row + (ch0 + i) * (kRows * 16), peer_x_full, __uint_as_float(ra[4 * i]),
-                    __uint_as_float(ra[4 * i + 1]), __uint_as_float(ra[4 * i + 2]),
-                    __uint_as_float(ra[4 * i + 3]));
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        st_async_v4(peer_x_row + (ch0 + 8 + i) * (kRows * 16), peer_x_full,
-                    __uint_as_float(rb[4 * i]), __uint_as_float(rb[4 * i + 1]),
-                    __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
-      if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[xb_i]), kXBytes);
-      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
-      if (!(ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), xb_par, kTimeoutPeer, abort)))
-        break;
-      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
+      // After a failed bounded wait a warp keeps iterating with the work skipped (later waits
+      // fail at once through the abort flag), so every softmax warp reaches each named
+      // barrier equally often and none is left in bar.sync.
+      ok = ok && warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort);
+      uint32_t ra[32], rb[32];
       float gmax = -INFINITY;
+      if (ok) {
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(6, j);
+        tc_fence_after();
+        tmem_ld32(t_row + kSCol + cbase, ra);
+        tmem_ld32(t_row + kSCol + cbase + 32, rb);
+        tmem_ld_wait();
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(18, j);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(lead_s_free);
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
+        if (kXBufs == 1 && j >= 1) {
+          // single buffer: it held P of tile j-1; free once that P.V completed
+          ok = warp_mbar_wait(smem_u32(&bars.pv_done[0]), (j - 1) & 1, kTimeoutMmaDone, abort);
+          if (ok && sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
+          if (ok && lane == 0) mbar_arrive_remote(peer_x_empty);
+        }
+      }
+      if (ok && j >= kXBufs)
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (j - kXBufs) & 1, kTimeoutExchange, abort);
+      if (ok) {
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(ch0 + i, row));
+        for (int i = 0; i < 8; ++i)
+          st_async_v4(peer_x_row + (ch0 + i) * (kRows * 16), peer_x_full, __uint_as_float(ra[4 * i]),
+                      __uint_as_float(ra[4 * i + 1]), __uint_as_float(ra[4 * i + 2]),
+                      __uint_as_float(ra[4 * i + 3]));
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = cbase + 4 * i + e;
-          uint32_t& rv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
-          const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
-          const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
-          gmax = fmaxf(gmax, t);
-          rv = __float_as_uint(t);
+        for (int i = 0; i < 8; ++i)
+          st_async_v4(peer_x_row + (ch0 + 8 + i) * (kRows * 16), peer_x_full,
+                      __uint_as_float(rb[4 * i]), __uint_as_float(rb[4 * i + 1]),
+                      __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
+        if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[xb_i]), kXBytes);
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), xb_par, kTimeoutPeer, abort);
+      }
+      if (ok) {
+        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(ch0 + i, row));
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = cbase + 4 * i + e;
+            uint32_t& rv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
+            const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
+            const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
+            gmax = fmaxf(gmax, t);
+            rv = __float_as_uint(t);
+          }
         }
       }
       red[grp][row] = gmax;
@@ -394,6 +400,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int g = 1; g < kGroups; ++g) tmax = fmaxf(tmax, red[g][row]);
       named_bar_sync(2 + quad, 32 * kGroups);
+      if (!ok) continue;
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(15, j);
       m_true = fmaxf(m_true, tmax);
       float alpha = 1.f;
@@ -407,7 +414,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) % kXBufs]),
                                   static_cast<uint32_t>((j - 1) / kXBufs) & 1u, kTimeoutMmaDone,
                                   abort)))
-          break;
+          continue;
         tc_fence_after();
         for (int c = grp; c < dh / 32; c += kGroups) {
           uint32_t o[32];
@@ -446,7 +453,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j + 1) % kXBufs]),
                                   static_cast<uint32_t>((j - 1) / kXBufs) & 1u, kTimeoutMmaDone,
                                   abort)))
-          break;
+          continue;
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
         if (lane == 0) mbar_arrive_remote(peer_x_empty);
       }
