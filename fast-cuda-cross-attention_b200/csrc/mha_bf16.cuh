@@ -8,8 +8,11 @@
 // One CTA owns 128 query rows of one (batch, head); a head dimension of at most 128 leaves
 // TMEM room for two CTAs per SM (256 columns each: two S tiles of 64 keys at columns 0..127,
 // O at 128..128+dh), so the two CTAs' softmax and tensor phases overlap without any cross-CTA
-// protocol.  S is double-buffered in TMEM (columns 0..63 and 64..127), so Q K^T of the next
-// tile never waits for the softmax warps to read the current one.  Per CTA:
+// protocol.  S is double-buffered in TMEM (columns 0..63 and 64..127).  The softmax warps
+// write P (bf16, two per 32-bit column) over the first 32 columns of its own S buffer, and
+// P V reads A from TMEM (tcgen05.mma .ts form); tcgen05 MMAs issued by one thread execute in
+// issue order, so Q K^T of tile t+2, issued after P V of tile t, overwrites that buffer
+// only after P V consumed it.  Per CTA:
 //   warp 0      TMA producer: Q once (resident), then K and V tiles of 64 keys through a
 //               3-stage ring in the order K(0), then per tile K(j+1), V(j)
 //   warp 1      MMA issuer: S = Q K^T (M=128, N=64, K=dh), O += P V (M=128, N=dh, K=64)
@@ -20,8 +23,6 @@
 //   K   K-major, boxes of 64 keys x 64 columns
 //   V   MN-major (rows are keys): the same boxes; the descriptor walks keys in 8-row groups
 //       (SBO 1024 B) and head columns in 64-wide groups (LBO = one box, 8 KB)
-//   P   K-major, 128 rows x 64 keys, written by the softmax warps (bf16), two buffers so the
-//       softmax of tile j+1 does not wait for O += P V of tile j
 // The barriers live at the end of the dynamic shared memory: with no static shared memory
 // the dynamic region starts 1024-byte aligned (checked at run time), which leaves room for
 // two CTAs of 112 KB per SM.
@@ -48,10 +49,8 @@ constexpr int kMaxBoxes = 2;                          // head_dim <= 128
 constexpr int kQBytes = kMaxBoxes * kRows * 128;      // 32 KB
 constexpr int kBoxBytes = kKeys * 128;                // 8 KB: 64 keys x 64 columns
 constexpr int kStageBytes = kMaxBoxes * kBoxBytes;    // 16 KB: a K tile or a V tile
-constexpr int kStages = 3;
-constexpr int kPBytes = kRows * 128;                  // 16 KB per buffer
-constexpr int kPBufs = 2;
-constexpr int kBarOffset = kQBytes + kStages * kStageBytes + kPBufs * kPBytes;
+constexpr int kStages = 5;
+constexpr int kBarOffset = kQBytes + kStages * kStageBytes;
 constexpr int kOnesOffset = kBarOffset + 256;   // 8 rows x 16 B of bf16 ones
 constexpr int kSmemBytes = kOnesOffset + 128;
 constexpr int kThreads = 192;
@@ -78,9 +77,8 @@ struct __align__(8) Barriers {
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t s_full[2];  // S buffer b holds the scores of tile j (j % 2 == b)
-  uint64_t s_free[2];  // the softmax warps copied S buffer b out of TMEM
-  uint64_t p_full;      // P of the current tile is in shared memory
-  uint64_t pv_done[2];  // O += P V of a tile using P buffer b completed (buffer free, O current)
+  uint64_t p_full;      // P of the current tile is in TMEM (over its S)
+  uint64_t pv_done;     // O += P V of the current tile completed (O current)
   uint64_t o_done;      // last P V completed
   uint32_t tmem_slot;
   int abort_flag;
@@ -112,7 +110,6 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   }
   uint8_t* qs = smem;
   uint8_t* stages = smem + kQBytes;
-  uint8_t* ps = stages + kStages * kStageBytes;
   Barriers& bars = *reinterpret_cast<Barriers*>(smem + kBarOffset);
   uint32_t& tmem_slot = bars.tmem_slot;
   int& abort_flag = bars.abort_flag;
@@ -136,13 +133,9 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_u32(&bars.s_full[i]), 1);
-      mbar_init(smem_u32(&bars.s_free[i]), kSoftmaxWarps);
-    }
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars.s_full[i]), 1);
     mbar_init(smem_u32(&bars.p_full), kSoftmaxWarps);
-    mbar_init(smem_u32(&bars.pv_done[0]), 1);
-    mbar_init(smem_u32(&bars.pv_done[1]), 1);
+    mbar_init(smem_u32(&bars.pv_done), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
     fence_mbar_init();
   }
@@ -229,11 +222,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       for (int j = 0; j < n_tiles && ok; ++j) {
         const int t = j + 1;
         if (t < n_tiles) {
-          // buffer t % 2 last held tile t - 2: wait until the softmax warps read it
-          if (t >= 2 && !(ok = mbar_wait(smem_u32(&bars.s_free[t & 1]), ((t >> 1) - 1) & 1,
-                                         kTimeoutSoftmax, abort)))
-            break;
-          tc_fence_after();
+          // buffer t % 2 last held P of tile t - 2, read by P V of tile t - 2, issued before
           mma_qk(t);
           if (!ok) break;
         }
@@ -244,13 +233,13 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         const uint32_t st = smem_u32(stages + s * kStageBytes);
 #pragma unroll
         for (int ks = 0; ks < kKeys / 16; ++ks) {
-          const uint64_t ad = smem_desc(smem_u32(ps + (j & 1) * kPBytes) + ks * 32, 16, 1024, kSw128);
+          const uint32_t a_tmem = tmem + kSCol + (j & 1) * kKeys + ks * 8;  // 16 keys of P
           const uint64_t bd = smem_desc(st + ks * 2048, kBoxBytes, 1024, kSw128);
-          mma_f16_ss(tmem + kOCol, ad, bd, idesc_pv, (j | ks) != 0);
-          if (kTcSum) mma_f16_ss(tmem + kOCol + p.dh, ad, ones_desc, idesc_sum, (j | ks) != 0);
+          mma_f16_ts(tmem + kOCol, a_tmem, bd, idesc_pv, (j | ks) != 0);
+          if (kTcSum) mma_f16_ts(tmem + kOCol + p.dh, a_tmem, ones_desc, idesc_sum, (j | ks) != 0);
         }
         mma_commit(smem_u32(&bars.empty[s]));
-        mma_commit(smem_u32(&bars.pv_done[j & 1]));
+        mma_commit(smem_u32(&bars.pv_done));
         XATTN_TRACE_POINT(4, j);
         if (++s == kStages) { s = 0; phase ^= 1u; }
       }
@@ -283,9 +272,6 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           x[k + 32] = __uint_as_float(sb[k]);
         }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars.s_free[sbuf]));
       if (warp == 2 && lane == 0) XATTN_TRACE_POINT(7, j);
       if (valid < kKeys) {  // ragged last tile: keys past N_input get weight 0
 #pragma unroll
@@ -308,15 +294,10 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         alpha = ex2_approx(m_run - tmax);
         m_run = tmax;
       }
-      // P buffer j % 2 is read by P V of tile j - 2 until that completes
-      if (j >= 2 && !(ok = warp_mbar_wait(smem_u32(&bars.pv_done[j & 1]), ((j >> 1) - 1) & 1,
-                                         kTimeoutMmaDone, abort)))
-        break;
       if (warp == 2 && lane == 0) XATTN_TRACE_POINT(8, j);
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
         // rescaling O needs every earlier P V complete: the last one is tile j - 1
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) & 1]), ((j - 1) >> 1) & 1,
-                                  kTimeoutMmaDone, abort)))
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done), (j - 1) & 1, kTimeoutMmaDone, abort)))
           break;
         tc_fence_after();
         for (int c = 0; c < p.dh / 32; ++c) {
@@ -342,22 +323,17 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       // mean of V (summing the unrounded weights doubles the error when a few keys dominate)
       const float neg_m = -m_run;
       float lsum = 0.f;
-      uint8_t* prow = ps + (j & 1) * kPBytes + row * 128;
+      uint32_t w[32];  // P of this row: column c holds keys 2c (low half) and 2c + 1
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 16-byte chunk c holds keys 8c .. 8c+7
-        uint32_t w[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int k0 = 8 * c + 2 * e;
-          const float p0 = ex2_approx(fmaf(x[k0], p.scale_log2, neg_m));
-          const float p1 = ex2_approx(fmaf(x[k0 + 1], p.scale_log2, neg_m));
-          w[e] = pack_bf16x2(p0, p1);
-          if (!kTcSum) lsum += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xffff0000u);
-        }
-        *reinterpret_cast<uint4*>(prow + ((c ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      for (int c = 0; c < 32; ++c) {
+        const float p0 = ex2_approx(fmaf(x[2 * c], p.scale_log2, neg_m));
+        const float p1 = ex2_approx(fmaf(x[2 * c + 1], p.scale_log2, neg_m));
+        w[c] = pack_bf16x2(p0, p1);
+        if (!kTcSum) lsum += __uint_as_float(w[c] << 16) + __uint_as_float(w[c] & 0xffff0000u);
       }
+      tmem_st32(t_row + kSCol + sbuf * kKeys, w);
+      tmem_st_wait();
       l_run = l_run * alpha + lsum;
-      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars.p_full));
