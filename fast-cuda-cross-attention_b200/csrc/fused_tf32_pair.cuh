@@ -17,6 +17,14 @@
 // leader's commits are multicast to both CTAs (empty, s_full, pv_done, o_done); the
 // softmax warps of both CTAs release S and publish P by one arrival per warp on the
 // leader's s_free / p_full barriers.  No TMA multicast is used.
+//
+// Operand ring.  Three producer warps share one ring of 24 KB stages in the order QK(0),
+// then per tile QK(j+1), V(j): a Q/K stage is a 32-column chunk of the CTA's 128 Q rows and
+// of its half of the K tile, a V stage one 4-D box of 32 keys x the CTA's 32-column slabs.
+// Producer 0 also prefetches into L2 the V of the tile being loaded and each producer the
+// next tile's K chunk it will load, so fewer stage round trips wait on DRAM.  The stream of
+// stages through this ring, not the softmax, sets the pace of the kernel: its depth is
+// bounded by the 128 KB of exchange / P buffers beside it.
 #pragma once
 
 #include "fused_tf32.cuh"
@@ -41,8 +49,9 @@ using fused::x_offset;
 
 constexpr int kVKeys = 32;           // keys per V chunk (four K=8 steps)
 constexpr int kStageBytes = 24576;   // Q chunk 16 KB + K half 8 KB, or a V chunk
-// Exchange / P buffers: 1 (deep ring: 6 stages, 144 KB of operands in flight) or 2 (the
-// next tile's exchange overlaps this tile's P.V; 4 stages).
+// Exchange / P buffers: 2 (the next tile's exchange overlaps this tile's P.V; 4 stages), or
+// 1 (a 6-stage ring, 144 KB of operands in flight, but the exchange then waits for P.V:
+// measured 10 % slower at the headline shape).
 constexpr int kXBufs = 2;
 constexpr int kStages = kXBufs == 1 ? 6 : 4;
 // Warps: 0 producer, 1 MMA issuer, 2..9 softmax, 10.. further producers.  Registers are
