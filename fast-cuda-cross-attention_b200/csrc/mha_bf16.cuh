@@ -65,6 +65,7 @@ struct Params {
   __nv_bfloat16* out;
   int heads, n_latent, n_input, dh, ld;  // ld = heads * dh elements per row
   int n_row_blocks;
+  int n_items;                           // B * heads * n_row_blocks
   float scale_log2;
 };
 
@@ -73,11 +74,15 @@ __host__ __device__ constexpr bool supports_dh(int dh) {
 }
 
 struct __align__(8) Barriers {
-  uint64_t q_full;
+  uint64_t q_full;      // Q of the current item landed
+  uint64_t q_empty;     // the current item's last Q K^T completed (Q buffer free)
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t s_full[2];  // S buffer b holds the scores of tile j (j % 2 == b)
-  uint64_t p_full;      // P of the current tile is in TMEM (over its S)
+  uint64_t p_full[2];   // P of tile g is in TMEM (over its S): barrier g % 2.  One per S
+                        // buffer: Q K^T of tile g + 1 is issued before P V of tile g, so a
+                        // warp can finish tile g + 1 while another is still on tile g; with a
+                        // single counter its second arrival would complete tile g's phase
   uint64_t pv_done;     // O += P V of the current tile completed (O current)
   uint64_t o_done;      // last P V completed
   uint32_t tmem_slot;
@@ -116,25 +121,30 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int rb = blockIdx.x % p.n_row_blocks;
-  const int bh = blockIdx.x / p.n_row_blocks;
-  const int h = bh % p.heads;
-  const int b = bh / p.heads;
-  const int row0 = rb * kRows;
-  const int col0 = h * p.dh;
-  const int n_tiles = (p.n_input + kKeys - 1) / kKeys;
+  const int n_tiles = (p.n_input + kKeys - 1) / kKeys;  // >= 1: the host skips N_input == 0
   const int n_boxes = (p.dh + kBoxCols - 1) / kBoxCols;
+  // Persistent: this CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ...  The tile loop
+  // runs on a global tile index g = (local item count) * n_tiles + j, which picks the S
+  // buffer and the parity of every per-tile barrier; per-item barriers use the item count.
+  struct Item {
+    int row0, col0, b;
+  };
+  auto item_at = [&](int item) {
+    const int rb = item % p.n_row_blocks, bh = item / p.n_row_blocks;
+    return Item{rb * kRows, (bh % p.heads) * p.dh, bh / p.heads};
+  };
   if (threadIdx.x == 0) XATTN_TRACE_POINT(14, 0);
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
     mbar_init(smem_u32(&bars.q_full), 1);
+    mbar_init(smem_u32(&bars.q_empty), 1);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
     for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars.s_full[i]), 1);
-    mbar_init(smem_u32(&bars.p_full), kSoftmaxWarps);
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars.p_full[i]), kSoftmaxWarps);
     mbar_init(smem_u32(&bars.pv_done), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
     fence_mbar_init();
@@ -161,188 +171,201 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   if (warp == 0) {
     // ============================================================== TMA producer
     if (elect_one()) {
-      mbar_arrive_expect_tx(smem_u32(&bars.q_full), n_boxes * kRows * 128);
-      for (int c = 0; c < n_boxes; ++c)
-        tma_load_3d(smem_u32(qs + c * (kRows * 128)), &p.tq, smem_u32(&bars.q_full),
-                    col0 + c * kBoxCols, row0, b);
       int s = 0;
       uint32_t phase = 0;
       bool ok = true;
-      auto load = [&](const CUtensorMap* map, int tile) {
-        if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort))) return;
-        mbar_arrive_expect_tx(smem_u32(&bars.full[s]), n_boxes * kBoxBytes);
+      int it = 0;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
+        const Item w = item_at(item);
+        // the Q buffer is free once the previous item's last Q K^T completed
+        if (it > 0 && !(ok = mbar_wait(smem_u32(&bars.q_empty), (it - 1) & 1, kTimeoutStageFree, abort)))
+          break;
+        mbar_arrive_expect_tx(smem_u32(&bars.q_full), n_boxes * kRows * 128);
         for (int c = 0; c < n_boxes; ++c)
-          tma_load_3d(smem_u32(stages + s * kStageBytes + c * kBoxBytes), map,
-                      smem_u32(&bars.full[s]), col0 + c * kBoxCols, tile * kKeys, b);
-        if (++s == kStages) { s = 0; phase ^= 1u; }
-      };
-      load(&p.tk, 0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles) load(&p.tk, j + 1);
-        XATTN_TRACE_POINT(0, j + 1);
-        if (ok) load(&p.tv, j);
-        XATTN_TRACE_POINT(1, j);
+          tma_load_3d(smem_u32(qs + c * (kRows * 128)), &p.tq, smem_u32(&bars.q_full),
+                      w.col0 + c * kBoxCols, w.row0, w.b);
+        auto load = [&](const CUtensorMap* map, int tile) {
+          if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort))) return;
+          mbar_arrive_expect_tx(smem_u32(&bars.full[s]), n_boxes * kBoxBytes);
+          for (int c = 0; c < n_boxes; ++c)
+            tma_load_3d(smem_u32(stages + s * kStageBytes + c * kBoxBytes), map,
+                        smem_u32(&bars.full[s]), w.col0 + c * kBoxCols, tile * kKeys, w.b);
+          if (++s == kStages) { s = 0; phase ^= 1u; }
+        };
+        load(&p.tk, 0);
+        for (int j = 0; j < n_tiles && ok; ++j) {
+          if (j + 1 < n_tiles) load(&p.tk, j + 1);
+          if (ok) load(&p.tv, j);
+        }
       }
-      // every stage this CTA loaded is released by an MMA commit before the MMA warp
-      // finishes; wait for the last ones so no copy is in flight at exit
+      // every stage loaded is released by an MMA commit; wait for the last ones (and the
+      // last Q) so no copy is in flight at exit
       for (int i = 0; i < kStages; ++i) {
         if (--s < 0) { s = kStages - 1; phase ^= 1u; }
         mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, nullptr);
       }
-      mbar_wait(smem_u32(&bars.q_full), 0, kTimeoutDrain, nullptr);
+      if (it > 0) mbar_wait(smem_u32(&bars.q_full), (it - 1) & 1, kTimeoutDrain, nullptr);
     }
   } else if (warp == 1) {
     // ============================================================== MMA issuer
     if (elect_one()) {
       int s = 0;
       uint32_t phase = 0;
-      bool ok = mbar_wait(smem_u32(&bars.q_full), 0, kTimeoutTmaFull, abort);
-      tc_fence_after();
+      bool ok = true;
       const uint32_t idesc_qk = instr_desc(1, kRows, kKeys, false, false);
       const uint32_t idesc_pv = instr_desc(1, kRows, p.dh, false, true);
       const uint32_t idesc_sum = instr_desc(1, kRows, 16, false, false);
       const uint64_t ones_desc = smem_desc(smem_u32(smem + kOnesOffset), 0, 0, kSwNone);
       const int ksteps_qk = p.dh / 16;
-      auto mma_qk = [&](int t) {  // S of tile t into buffer t % 2
-        if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) return;
+      int it = 0;
+      for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
+        const int g0 = it * n_tiles;
+        if (!(ok = mbar_wait(smem_u32(&bars.q_full), it & 1, kTimeoutTmaFull, abort))) break;
         tc_fence_after();
-        const uint32_t st = smem_u32(stages + s * kStageBytes);
-        for (int ks = 0; ks < ksteps_qk; ++ks) {
-          const int c = ks >> 2, off = (ks & 3) * 32;
-          const uint64_t ad = smem_desc(smem_u32(qs) + c * (kRows * 128) + off, 16, 1024, kSw128);
-          const uint64_t bd = smem_desc(st + c * kBoxBytes + off, 16, 1024, kSw128);
-          mma_f16_ss(tmem + kSCol + (t & 1) * kKeys, ad, bd, idesc_qk, ks != 0);
-        }
-        mma_commit(smem_u32(&bars.empty[s]));
-        mma_commit(smem_u32(&bars.s_full[t & 1]));
-        XATTN_TRACE_POINT(2, t);
-        if (++s == kStages) { s = 0; phase ^= 1u; }
-      };
-      if (ok && n_tiles > 0) mma_qk(0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        const int t = j + 1;
-        if (t < n_tiles) {
-          // buffer t % 2 last held P of tile t - 2, read by P V of tile t - 2, issued before
-          mma_qk(t);
-          if (!ok) break;
-        }
-        if (!(ok = mbar_wait(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
-        XATTN_TRACE_POINT(3, j);
-        if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
-        tc_fence_after();
-        const uint32_t st = smem_u32(stages + s * kStageBytes);
+        auto mma_qk = [&](int j) {  // S of tile g0 + j into buffer (g0 + j) % 2
+          if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) return;
+          tc_fence_after();
+          const uint32_t st = smem_u32(stages + s * kStageBytes);
+          for (int ks = 0; ks < ksteps_qk; ++ks) {
+            const int c = ks >> 2, off = (ks & 3) * 32;
+            const uint64_t ad = smem_desc(smem_u32(qs) + c * (kRows * 128) + off, 16, 1024, kSw128);
+            const uint64_t bd = smem_desc(st + c * kBoxBytes + off, 16, 1024, kSw128);
+            mma_f16_ss(tmem + kSCol + ((g0 + j) & 1) * kKeys, ad, bd, idesc_qk, ks != 0);
+          }
+          mma_commit(smem_u32(&bars.empty[s]));
+          mma_commit(smem_u32(&bars.s_full[(g0 + j) & 1]));
+          if (j == n_tiles - 1) mma_commit(smem_u32(&bars.q_empty));  // Q no longer read
+          if (++s == kStages) { s = 0; phase ^= 1u; }
+        };
+        // buffer (g0 + j) % 2 last held P of tile g0 + j - 2, read by a P V issued earlier
+        mma_qk(0);
+        for (int j = 0; j < n_tiles && ok; ++j) {
+          const int g = g0 + j;
+          if (j + 1 < n_tiles) {
+            mma_qk(j + 1);
+            if (!ok) break;
+          }
+          // P of tile g; for j == 0 also: the epilogue of the previous item read O
+          if (!(ok = mbar_wait(smem_u32(&bars.p_full[g & 1]), (g >> 1) & 1, kTimeoutSoftmax, abort)))
+            break;
+          if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
+          tc_fence_after();
+          const uint32_t st = smem_u32(stages + s * kStageBytes);
 #pragma unroll
-        for (int ks = 0; ks < kKeys / 16; ++ks) {
-          const uint32_t a_tmem = tmem + kSCol + (j & 1) * kKeys + ks * 8;  // 16 keys of P
-          const uint64_t bd = smem_desc(st + ks * 2048, kBoxBytes, 1024, kSw128);
-          mma_f16_ts(tmem + kOCol, a_tmem, bd, idesc_pv, (j | ks) != 0);
-          if (kTcSum) mma_f16_ts(tmem + kOCol + p.dh, a_tmem, ones_desc, idesc_sum, (j | ks) != 0);
+          for (int ks = 0; ks < kKeys / 16; ++ks) {
+            const uint32_t a_tmem = tmem + kSCol + (g & 1) * kKeys + ks * 8;  // 16 keys of P
+            const uint64_t bd = smem_desc(st + ks * 2048, kBoxBytes, 1024, kSw128);
+            mma_f16_ts(tmem + kOCol, a_tmem, bd, idesc_pv, (j | ks) != 0);
+            if (kTcSum) mma_f16_ts(tmem + kOCol + p.dh, a_tmem, ones_desc, idesc_sum, (j | ks) != 0);
+          }
+          mma_commit(smem_u32(&bars.empty[s]));
+          mma_commit(smem_u32(&bars.pv_done));
+          if (++s == kStages) { s = 0; phase ^= 1u; }
         }
-        mma_commit(smem_u32(&bars.empty[s]));
-        mma_commit(smem_u32(&bars.pv_done));
-        XATTN_TRACE_POINT(4, j);
-        if (++s == kStages) { s = 0; phase ^= 1u; }
+        mma_commit(smem_u32(&bars.o_done));
       }
-      mma_commit(smem_u32(&bars.o_done));
     }
   } else {
     // ============================================================== softmax + epilogue
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
-    float m_run = -INFINITY;
-    float l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int valid = min(kKeys, p.n_input - j * kKeys);
-      const int sbuf = j & 1;
-      if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full[sbuf]), (j >> 1) & 1, kTimeoutMmaDone, abort)))
-        break;
-      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(6, j);
-      tc_fence_after();
-      float x[kKeys];  // raw scores of this row
-      {
-        uint32_t sa[32], sb[32];
-        tmem_ld32(t_row + kSCol + sbuf * kKeys, sa);
-        tmem_ld32(t_row + kSCol + sbuf * kKeys + 32, sb);
-        tmem_ld_wait();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          x[k] = __uint_as_float(sa[k]);
-          x[k + 32] = __uint_as_float(sb[k]);
-        }
-      }
-      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(7, j);
-      if (valid < kKeys) {  // ragged last tile: keys past N_input get weight 0
-#pragma unroll
-        for (int k = 0; k < kKeys; ++k) x[k] = k < valid ? x[k] : -INFINITY;
-      }
-      // row maximum of the raw scores (the scale is positive), four independent chains
-      float mx[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        mx[c] = x[16 * c];
-#pragma unroll
-        for (int k = 1; k < 15; k += 2) mx[c] = fmax3(mx[c], x[16 * c + k], x[16 * c + k + 1]);
-        mx[c] = fmaxf(mx[c], x[16 * c + 15]);
-      }
-      const float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * p.scale_log2;
-      float alpha = 1.f;
-      if (j == 0) {
-        m_run = tmax;
-      } else if (tmax > m_run + kRescaleLog2) {
-        alpha = ex2_approx(m_run - tmax);
-        m_run = tmax;
-      }
-      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(8, j);
-      if (__any_sync(0xffffffffu, alpha != 1.f)) {
-        // rescaling O needs every earlier P V complete: the last one is tile j - 1
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done), (j - 1) & 1, kTimeoutMmaDone, abort)))
+    int it = 0;
+    for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
+      const Item wi = item_at(item);
+      const int g0 = it * n_tiles;
+      float m_run = -INFINITY;
+      float l_run = 0.f;
+      for (int j = 0; j < n_tiles; ++j) {
+        const int g = g0 + j;
+        const int valid = min(kKeys, p.n_input - j * kKeys);
+        const int sbuf = g & 1;
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.s_full[sbuf]), (g >> 1) & 1, kTimeoutMmaDone, abort)))
           break;
         tc_fence_after();
-        for (int c = 0; c < p.dh / 32; ++c) {
-          uint32_t o[32];
-          tmem_ld32(t_row + kOCol + c * 32, o);
+        float x[kKeys];  // raw scores of this row
+        {
+          uint32_t sa[32], sb[32];
+          tmem_ld32(t_row + kSCol + sbuf * kKeys, sa);
+          tmem_ld32(t_row + kSCol + sbuf * kKeys + 32, sb);
           tmem_ld_wait();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(t_row + kOCol + c * 32, o);
+          for (int k = 0; k < 32; ++k) {
+            x[k] = __uint_as_float(sa[k]);
+            x[k + 32] = __uint_as_float(sb[k]);
+          }
         }
-        if (kTcSum) {  // the row-sum columns scale with O
-          uint32_t o[16];
-          tmem_ld16(t_row + kOCol + p.dh, o);
-          tmem_ld_wait();
+        if (valid < kKeys) {  // ragged last tile: keys past N_input get weight 0
 #pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st16(t_row + kOCol + p.dh, o);
+          for (int k = 0; k < kKeys; ++k) x[k] = k < valid ? x[k] : -INFINITY;
         }
+        // row maximum of the raw scores (the scale is positive), four independent chains
+        float mx[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          mx[c] = x[16 * c];
+#pragma unroll
+          for (int k = 1; k < 15; k += 2) mx[c] = fmax3(mx[c], x[16 * c + k], x[16 * c + k + 1]);
+          mx[c] = fmaxf(mx[c], x[16 * c + 15]);
+        }
+        const float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * p.scale_log2;
+        float alpha = 1.f;
+        if (j == 0) {
+          m_run = tmax;
+        } else if (tmax > m_run + kRescaleLog2) {
+          alpha = ex2_approx(m_run - tmax);
+          m_run = tmax;
+        }
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+          // rescaling O needs every earlier P V complete: the last one is tile g - 1
+          if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done), (g - 1) & 1, kTimeoutMmaDone, abort)))
+            break;
+          tc_fence_after();
+          for (int c = 0; c < p.dh / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_row + kOCol + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_row + kOCol + c * 32, o);
+          }
+          if (kTcSum) {  // the row-sum columns scale with O
+            uint32_t o[16];
+            tmem_ld16(t_row + kOCol + p.dh, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(t_row + kOCol + p.dh, o);
+          }
+          tmem_st_wait();
+        }
+        // weights 2^(x * scale_log2 - m): one FFMA and one ex2 per score.  The row sum adds
+        // the bf16-rounded weights the P.V product uses, so each output row is an exact
+        // weighted mean of V (summing the unrounded weights doubles the error when a few keys
+        // dominate)
+        const float neg_m = -m_run;
+        float lsum = 0.f;
+        uint32_t w[32];  // P of this row: column c holds keys 2c (low half) and 2c + 1
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = ex2_approx(fmaf(x[2 * c], p.scale_log2, neg_m));
+          const float p1 = ex2_approx(fmaf(x[2 * c + 1], p.scale_log2, neg_m));
+          w[c] = pack_bf16x2(p0, p1);
+          if (!kTcSum) lsum += __uint_as_float(w[c] << 16) + __uint_as_float(w[c] & 0xffff0000u);
+        }
+        tmem_st32(t_row + kSCol + sbuf * kKeys, w);
         tmem_st_wait();
+        l_run = l_run * alpha + lsum;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bars.p_full[sbuf]));
       }
-      // weights 2^(x * scale_log2 - m): one FFMA and one ex2 per score.  The row sum adds the
-      // bf16-rounded weights the P.V product uses, so each output row is an exact weighted
-      // mean of V (summing the unrounded weights doubles the error when a few keys dominate)
-      const float neg_m = -m_run;
-      float lsum = 0.f;
-      uint32_t w[32];  // P of this row: column c holds keys 2c (low half) and 2c + 1
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float p0 = ex2_approx(fmaf(x[2 * c], p.scale_log2, neg_m));
-        const float p1 = ex2_approx(fmaf(x[2 * c + 1], p.scale_log2, neg_m));
-        w[c] = pack_bf16x2(p0, p1);
-        if (!kTcSum) lsum += __uint_as_float(w[c] << 16) + __uint_as_float(w[c] & 0xffff0000u);
-      }
-      tmem_st32(t_row + kSCol + sbuf * kKeys, w);
-      tmem_st_wait();
-      l_run = l_run * alpha + lsum;
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars.p_full));
-      if (warp == 2 && lane == 0) XATTN_TRACE_POINT(10, j);
-    }
-    // ---- epilogue: O / l -> bf16
-    if (ok && n_tiles > 0 && warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
+      // ---- epilogue: O / l -> bf16; reading O precedes the next item's first P V, which
+      // waits for this warp's next p_full arrival
+      if (!ok || !(ok = warp_mbar_wait(smem_u32(&bars.o_done), it & 1, kTimeoutMmaDone, abort))) break;
       tc_fence_after();
-      const int grow = row0 + row;
+      const int grow = wi.row0 + row;
       float l_tot = l_run;
       if (kTcSum) {
         uint32_t lr[16];
@@ -351,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         l_tot = __uint_as_float(lr[0]);
       }
       const float inv = 1.f / l_tot;
-      __nv_bfloat16* dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.ld + col0;
+      __nv_bfloat16* dst = p.out + (static_cast<size_t>(wi.b) * p.n_latent + grow) * p.ld + wi.col0;
       for (int c = 0; c < p.dh / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(t_row + kOCol + c * 32, o);
@@ -367,6 +390,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
                 pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
         }
       }
+      tc_fence_before();
     }
   }
 

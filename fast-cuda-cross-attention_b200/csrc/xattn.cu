@@ -705,9 +705,10 @@ extern "C" int xattn_lse_finalize(const float* ol, float* output, long long rows
 }
 
 // Multi-head bf16 tensor-core kernel (mha_bf16.cuh): heads side by side in rows of
-// heads * head_dim elements.
+// heads * head_dim elements.  Persistent: two CTAs per SM (the kernel's occupancy) loop
+// over the B * heads * row-block items.
 int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
-                    __nv_bfloat16* out, int B, int Nl, int Ni, int heads, int dh,
+                    __nv_bfloat16* out, int B, int Nl, int Ni, int heads, int dh, int sms,
                     cudaStream_t stream) {
   mha::Params p;
   const uint64_t ld = static_cast<uint64_t>(heads) * dh;
@@ -732,8 +733,10 @@ int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_b
   p.ld = static_cast<int>(ld);
   p.n_row_blocks = (Nl + mha::kRows - 1) / mha::kRows;
   p.scale_log2 = static_cast<float>(kLog2e / std::sqrt(static_cast<double>(dh)));
-  const long long ctas = static_cast<long long>(B) * heads * p.n_row_blocks;
-  if (ctas > 0x7fffffffLL) return XATTN_ERR_ARG;
+  const long long items = static_cast<long long>(B) * heads * p.n_row_blocks;
+  if (items > 0x7fffffffLL) return XATTN_ERR_ARG;
+  p.n_items = static_cast<int>(items);
+  const long long ctas = std::min<long long>(items, 2LL * sms);
   if (mha::tc_sum_for(dh))
     mha::mha_bf16_kernel<true><<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
   else
@@ -754,7 +757,7 @@ extern "C" int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K,
   if (g_opt_path.load() != 2 && mha::supports_dh(head_dim) && aligned16(Q) && aligned16(K) &&
       aligned16(V) && aligned16(output) && static_cast<long long>(heads) * head_dim <= 0x7fffffff)
     return set_error(launch_mha_bf16(Q, K, V, output, batch_size, N_latent, N_input, heads,
-                                     head_dim, stream));
+                                     head_dim, sm_count(dev), stream));
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(head_dim));
   return set_error(launch_simt<__nv_bfloat16, __nv_bfloat16>(
       Q, K, V, output, nullptr, nullptr, nullptr, batch_size, heads, N_latent, N_input, head_dim, 1,
