@@ -300,22 +300,49 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
 #pragma unroll
           for (int k = 0; k < kKeys; ++k) x[k] = k < valid ? x[k] : -INFINITY;
         }
+        // weights 2^(x * scale_log2 - m): one FFMA and one ex2 per score.  The row sum adds
+        // the bf16-rounded weights the P.V product uses, so each output row is an exact
+        // weighted mean of V (summing the unrounded weights doubles the error when a few keys
+        // dominate)
+        float lsum;
+        uint32_t w[32];  // P of this row: column c holds keys 2c (low half) and 2c + 1
+        auto weights = [&](float neg_m) {
+          lsum = 0.f;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float p0 = ex2_approx(fmaf(x[2 * c], p.scale_log2, neg_m));
+            const float p1 = ex2_approx(fmaf(x[2 * c + 1], p.scale_log2, neg_m));
+            w[c] = pack_bf16x2(p0, p1);
+            if (!kTcSum) lsum += __uint_as_float(w[c] << 16) + __uint_as_float(w[c] & 0xffff0000u);
+          }
+        };
         // row maximum of the raw scores (the scale is positive), four independent chains
-        float mx[4];
+        auto row_max = [&]() {
+          float mx[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          mx[c] = x[16 * c];
+          for (int c = 0; c < 4; ++c) {
+            mx[c] = x[16 * c];
 #pragma unroll
-          for (int k = 1; k < 15; k += 2) mx[c] = fmax3(mx[c], x[16 * c + k], x[16 * c + k + 1]);
-          mx[c] = fmaxf(mx[c], x[16 * c + 15]);
-        }
-        const float tmax = fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * p.scale_log2;
+            for (int k = 1; k < 15; k += 2) mx[c] = fmax3(mx[c], x[16 * c + k], x[16 * c + k + 1]);
+            mx[c] = fmaxf(mx[c], x[16 * c + 15]);
+          }
+          return fmaxf(fmax3(mx[0], mx[1], mx[2]), mx[3]) * p.scale_log2;
+        };
         float alpha = 1.f;
         if (j == 0) {
-          m_run = tmax;
-        } else if (tmax > m_run + kRescaleLog2) {
-          alpha = ex2_approx(m_run - tmax);
-          m_run = tmax;
+          m_run = row_max();
+          weights(-m_run);
+        } else {
+          // The running maximum changes only when a tile exceeds it by 2^kRescaleLog2 (lazy
+          // rescale), so the weights are computed against m_run while the tile maximum is
+          // found alongside: the ex2 stream does not wait for the maximum.  A tile that does
+          // exceed it (rare once a few tiles are in) recomputes its weights below.
+          weights(-m_run);
+          const float tmax = row_max();
+          if (tmax > m_run + kRescaleLog2) {
+            alpha = ex2_approx(m_run - tmax);
+            m_run = tmax;
+          }
         }
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
           // rescaling O needs every earlier P V complete: the last one is tile g - 1
@@ -339,20 +366,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
             tmem_st16(t_row + kOCol + p.dh, o);
           }
           tmem_st_wait();
-        }
-        // weights 2^(x * scale_log2 - m): one FFMA and one ex2 per score.  The row sum adds
-        // the bf16-rounded weights the P.V product uses, so each output row is an exact
-        // weighted mean of V (summing the unrounded weights doubles the error when a few keys
-        // dominate)
-        const float neg_m = -m_run;
-        float lsum = 0.f;
-        uint32_t w[32];  // P of this row: column c holds keys 2c (low half) and 2c + 1
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = ex2_approx(fmaf(x[2 * c], p.scale_log2, neg_m));
-          const float p1 = ex2_approx(fmaf(x[2 * c + 1], p.scale_log2, neg_m));
-          w[c] = pack_bf16x2(p0, p1);
-          if (!kTcSum) lsum += __uint_as_float(w[c] << 16) + __uint_as_float(w[c] & 0xffff0000u);
+          weights(-m_run);  // lanes whose maximum did not move recompute the same weights
         }
         tmem_st32(t_row + kSCol + sbuf * kKeys, w);
         tmem_st_wait();
