@@ -13,21 +13,24 @@
 // P V reads A from TMEM (tcgen05.mma .ts form); tcgen05 MMAs issued by one thread execute in
 // issue order, so Q K^T of tile t+2, issued after P V of tile t, overwrites that buffer
 // only after P V consumed it.  Per CTA:
-//   warp 0      TMA producer: Q once (resident), then K and V tiles of 64 keys through a
-//               3-stage ring in the order K(0), then per tile K(j+1), V(j)
+//   warp 0      TMA producer: Q once per item (resident), then K and V tiles of 64 keys
+//               through a ring in the order K(0), then per tile K(j+1), V(j)
 //   warp 1      MMA issuer: S = Q K^T (M=128, N=64, K=dh), O += P V (M=128, N=dh, K=64)
 //   warps 2..5  softmax, one query row per thread (warp w reads TMEM lanes 32*(w%4)..+31),
 //               then the epilogue
-// Operands in shared memory (128-byte swizzle, 64 bf16 per swizzle row):
-//   Q   K-major, ceil(dh/64) boxes of 128 rows x 64 columns
-//   K   K-major, boxes of 64 keys x 64 columns
+// Operands in shared memory, in boxes of bc columns: bc = 64 (128-byte swizzle rows) for
+// d >= 64, bc = 32 (64-byte swizzle rows) for d = 32.  At d = 96 the second box also holds
+// 32 columns of the next head (or zero fill past the last head) that the MMAs never read:
+// three 32-column boxes would move a quarter fewer bytes, but measured 20 % slower (the
+// tensor core's operand reads from 64-byte swizzle rows cost more than the bytes saved).
+//   Q   K-major, dh/bc boxes of 128 rows x bc columns
+//   K   K-major, boxes of 64 keys x bc columns
 //   V   MN-major (rows are keys): the same boxes; the descriptor walks keys in 8-row groups
-//       (SBO 1024 B) and head columns in 64-wide groups (LBO = one box, 8 KB)
-// The barriers live at the end of the dynamic shared memory: with no static shared memory
-// the dynamic region starts 1024-byte aligned (checked at run time), which leaves room for
-// two CTAs of 112 KB per SM.
-// A head dimension that is not a multiple of 64 loads the next head's (or out-of-range,
-// zero-filled) columns into the last box; the MMAs never read them.
+//       (SBO = 8 rows) and head columns in bc-wide groups (LBO = one box)
+// Q and the ring share a 112 KB operand area; the ring takes as many stages as fit (five at
+// d = 96 and 128, kMaxStages at d = 32 and 64).  The barriers live after it: with no static
+// shared memory the dynamic region starts 1024-byte aligned (checked at run time), which
+// leaves room for two CTAs per SM.
 // Row sums on the tensor core (kTcSum, d <= 112): with each P.V step the MMA issuer also
 // multiplies P by an all-ones B operand (N = 16), accumulating l = sum_k P[r, k] of the
 // bf16-rounded weights into TMEM columns 128+d .. 143+d; the softmax warps then do no
@@ -44,13 +47,11 @@ namespace mha {
 
 constexpr int kRows = 128;
 constexpr int kKeys = 64;
-constexpr int kBoxCols = 64;                          // bf16 per 128-byte row
-constexpr int kMaxBoxes = 2;                          // head_dim <= 128
-constexpr int kQBytes = kMaxBoxes * kRows * 128;      // 32 KB
-constexpr int kBoxBytes = kKeys * 128;                // 8 KB: 64 keys x 64 columns
-constexpr int kStageBytes = kMaxBoxes * kBoxBytes;    // 16 KB: a K tile or a V tile
-constexpr int kStages = 5;
-constexpr int kBarOffset = kQBytes + kStages * kStageBytes;
+// Operand area: Q (resident per item) followed by the K/V ring, whose stage count follows
+// from the head dimension's tile size (kMaxStages at most).
+constexpr int kOperandBytes = 112 * 1024;
+constexpr int kMaxStages = 8;
+constexpr int kBarOffset = kOperandBytes;
 constexpr int kOnesOffset = kBarOffset + 256;   // 8 rows x 16 B of bf16 ones
 constexpr int kSmemBytes = kOnesOffset + 128;
 constexpr int kThreads = 192;
@@ -61,7 +62,7 @@ constexpr int kOCol = 128;
 constexpr float kRescaleLog2 = 8.f;  // lazy rescale threshold (log2 units), as the fp32 kernels
 
 struct Params {
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv;  // boxes of Layout<dh>::kBc columns x (128 or kKeys) rows
   __nv_bfloat16* out;
   int heads, n_latent, n_input, dh, ld;  // ld = heads * dh elements per row
   int n_row_blocks;
@@ -70,14 +71,14 @@ struct Params {
 };
 
 __host__ __device__ constexpr bool supports_dh(int dh) {
-  return dh == 64 || dh == 96 || dh == 128;
+  return dh == 32 || dh == 64 || dh == 96 || dh == 128;
 }
 
 struct __align__(8) Barriers {
   uint64_t q_full;      // Q of the current item landed
   uint64_t q_empty;     // the current item's last Q K^T completed (Q buffer free)
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t s_full[2];  // S buffer b holds the scores of tile j (j % 2 == b)
   uint64_t p_full[2];   // P of tile g is in TMEM (over its S): barrier g % 2.  One per S
                         // buffer: Q K^T of tile g + 1 is issued before P V of tile g, so a
@@ -103,7 +104,27 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __host__ __device__ constexpr bool tc_sum_for(int dh) { return dh <= 112; }
 
-template <bool kTcSum>
+// Compile-time operand layout of one head dimension (the MMA issuer is a single thread on
+// the tensor pipe's critical path: its per-step address arithmetic must fold to constants).
+template <int kDh>
+struct Layout {
+  static constexpr bool kTcSum = tc_sum_for(kDh);
+  static constexpr int kBc = kDh >= 64 ? 64 : 32;            // columns per box
+  static constexpr int kRowB = 2 * kBc;                      // bytes per swizzle row
+  static constexpr uint32_t kSwz = kRowB == 128 ? kSw128 : kSw64;
+  static constexpr int kBoxes = (kDh + kBc - 1) / kBc;
+  static constexpr int kQBox = kRows * kRowB;
+  static constexpr int kKvBox = kKeys * kRowB;
+  static constexpr int kStageBytes = kBoxes * kKvBox;
+  static constexpr int kQBytes = kBoxes * kQBox;
+  static constexpr int kStages = (kOperandBytes - kQBytes) / kStageBytes < kMaxStages
+                                     ? (kOperandBytes - kQBytes) / kStageBytes
+                                     : kMaxStages;
+  static constexpr int kKStepsBox = kBc / 16;                // K steps of 16 per swizzle row
+  static_assert(kStages >= 2, "K/V ring needs two stages");
+};
+
+template <int kDh>
 __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   // swizzled TMA boxes and UMMA descriptors need 1024-byte alignment; the kernel has no
@@ -114,7 +135,12 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
     return;
   }
   uint8_t* qs = smem;
-  uint8_t* stages = smem + kQBytes;
+  using L = Layout<kDh>;
+  constexpr bool kTcSum = L::kTcSum;
+  constexpr int rowb = L::kRowB, n_boxes = L::kBoxes, q_box = L::kQBox, kv_box = L::kKvBox;
+  constexpr int stage_bytes = L::kStageBytes, n_stages = L::kStages;
+  constexpr uint32_t swz = L::kSwz;
+  uint8_t* stages = smem + L::kQBytes;
   Barriers& bars = *reinterpret_cast<Barriers*>(smem + kBarOffset);
   uint32_t& tmem_slot = bars.tmem_slot;
   int& abort_flag = bars.abort_flag;
@@ -122,7 +148,6 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int n_tiles = (p.n_input + kKeys - 1) / kKeys;  // >= 1: the host skips N_input == 0
-  const int n_boxes = (p.dh + kBoxCols - 1) / kBoxCols;
   // Persistent: this CTA takes items blockIdx.x, blockIdx.x + gridDim.x, ...  The tile loop
   // runs on a global tile index g = (local item count) * n_tiles + j, which picks the S
   // buffer and the parity of every per-tile barrier; per-item barriers use the item count.
@@ -131,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   };
   auto item_at = [&](int item) {
     const int rb = item % p.n_row_blocks, bh = item / p.n_row_blocks;
-    return Item{rb * kRows, (bh % p.heads) * p.dh, bh / p.heads};
+    return Item{rb * kRows, (bh % p.heads) * kDh, bh / p.heads};
   };
   if (threadIdx.x == 0) XATTN_TRACE_POINT(14, 0);
 
@@ -139,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
     abort_flag = 0;
     mbar_init(smem_u32(&bars.q_full), 1);
     mbar_init(smem_u32(&bars.q_empty), 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < n_stages; ++s) {
       mbar_init(smem_u32(&bars.full[s]), 1);
       mbar_init(smem_u32(&bars.empty[s]), 1);
     }
@@ -180,17 +205,17 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         // the Q buffer is free once the previous item's last Q K^T completed
         if (it > 0 && !(ok = mbar_wait(smem_u32(&bars.q_empty), (it - 1) & 1, kTimeoutStageFree, abort)))
           break;
-        mbar_arrive_expect_tx(smem_u32(&bars.q_full), n_boxes * kRows * 128);
+        mbar_arrive_expect_tx(smem_u32(&bars.q_full), n_boxes * q_box);
         for (int c = 0; c < n_boxes; ++c)
-          tma_load_3d(smem_u32(qs + c * (kRows * 128)), &p.tq, smem_u32(&bars.q_full),
-                      w.col0 + c * kBoxCols, w.row0, w.b);
+          tma_load_3d(smem_u32(qs + c * q_box), &p.tq, smem_u32(&bars.q_full),
+                      w.col0 + c * L::kBc, w.row0, w.b);
         auto load = [&](const CUtensorMap* map, int tile) {
           if (!(ok = mbar_wait(smem_u32(&bars.empty[s]), phase ^ 1u, kTimeoutStageFree, abort))) return;
-          mbar_arrive_expect_tx(smem_u32(&bars.full[s]), n_boxes * kBoxBytes);
+          mbar_arrive_expect_tx(smem_u32(&bars.full[s]), stage_bytes);
           for (int c = 0; c < n_boxes; ++c)
-            tma_load_3d(smem_u32(stages + s * kStageBytes + c * kBoxBytes), map,
-                        smem_u32(&bars.full[s]), w.col0 + c * kBoxCols, tile * kKeys, w.b);
-          if (++s == kStages) { s = 0; phase ^= 1u; }
+            tma_load_3d(smem_u32(stages + s * stage_bytes + c * kv_box), map,
+                        smem_u32(&bars.full[s]), w.col0 + c * L::kBc, tile * kKeys, w.b);
+          if (++s == n_stages) { s = 0; phase ^= 1u; }
         };
         load(&p.tk, 0);
         for (int j = 0; j < n_tiles && ok; ++j) {
@@ -200,8 +225,8 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       }
       // every stage loaded is released by an MMA commit; wait for the last ones (and the
       // last Q) so no copy is in flight at exit
-      for (int i = 0; i < kStages; ++i) {
-        if (--s < 0) { s = kStages - 1; phase ^= 1u; }
+      for (int i = 0; i < n_stages; ++i) {
+        if (--s < 0) { s = n_stages - 1; phase ^= 1u; }
         mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, nullptr);
       }
       if (it > 0) mbar_wait(smem_u32(&bars.q_full), (it - 1) & 1, kTimeoutDrain, nullptr);
@@ -213,10 +238,11 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       uint32_t phase = 0;
       bool ok = true;
       const uint32_t idesc_qk = instr_desc(1, kRows, kKeys, false, false);
-      const uint32_t idesc_pv = instr_desc(1, kRows, p.dh, false, true);
+      constexpr uint32_t idesc_pv = instr_desc(1, kRows, kDh, false, true);
       const uint32_t idesc_sum = instr_desc(1, kRows, 16, false, false);
       const uint64_t ones_desc = smem_desc(smem_u32(smem + kOnesOffset), 0, 0, kSwNone);
-      const int ksteps_qk = p.dh / 16;
+      constexpr int ksteps_qk = kDh / 16;
+      constexpr int ksteps_box = L::kKStepsBox;
       int it = 0;
       for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x, ++it) {
         const int g0 = it * n_tiles;
@@ -225,17 +251,18 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         auto mma_qk = [&](int j) {  // S of tile g0 + j into buffer (g0 + j) % 2
           if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) return;
           tc_fence_after();
-          const uint32_t st = smem_u32(stages + s * kStageBytes);
+          const uint32_t st = smem_u32(stages + s * stage_bytes);
+#pragma unroll
           for (int ks = 0; ks < ksteps_qk; ++ks) {
-            const int c = ks >> 2, off = (ks & 3) * 32;
-            const uint64_t ad = smem_desc(smem_u32(qs) + c * (kRows * 128) + off, 16, 1024, kSw128);
-            const uint64_t bd = smem_desc(st + c * kBoxBytes + off, 16, 1024, kSw128);
+            const int c = ks / ksteps_box, off = (ks % ksteps_box) * 32;
+            const uint64_t ad = smem_desc(smem_u32(qs) + c * q_box + off, 16, 8 * rowb, swz);
+            const uint64_t bd = smem_desc(st + c * kv_box + off, 16, 8 * rowb, swz);
             mma_f16_ss(tmem + kSCol + ((g0 + j) & 1) * kKeys, ad, bd, idesc_qk, ks != 0);
           }
           mma_commit(smem_u32(&bars.empty[s]));
           mma_commit(smem_u32(&bars.s_full[(g0 + j) & 1]));
           if (j == n_tiles - 1) mma_commit(smem_u32(&bars.q_empty));  // Q no longer read
-          if (++s == kStages) { s = 0; phase ^= 1u; }
+          if (++s == n_stages) { s = 0; phase ^= 1u; }
         };
         // buffer (g0 + j) % 2 last held P of tile g0 + j - 2, read by a P V issued earlier
         mma_qk(0);
@@ -250,17 +277,18 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
             break;
           if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
           tc_fence_after();
-          const uint32_t st = smem_u32(stages + s * kStageBytes);
+          const uint32_t st = smem_u32(stages + s * stage_bytes);
 #pragma unroll
           for (int ks = 0; ks < kKeys / 16; ++ks) {
             const uint32_t a_tmem = tmem + kSCol + (g & 1) * kKeys + ks * 8;  // 16 keys of P
-            const uint64_t bd = smem_desc(st + ks * 2048, kBoxBytes, 1024, kSw128);
+            // V MN-major: 16 keys = 16 swizzle rows; head columns step by a box (LBO)
+            const uint64_t bd = smem_desc(st + ks * 16 * rowb, kv_box, 8 * rowb, swz);
             mma_f16_ts(tmem + kOCol, a_tmem, bd, idesc_pv, (j | ks) != 0);
-            if (kTcSum) mma_f16_ts(tmem + kOCol + p.dh, a_tmem, ones_desc, idesc_sum, (j | ks) != 0);
+            if (kTcSum) mma_f16_ts(tmem + kOCol + kDh, a_tmem, ones_desc, idesc_sum, (j | ks) != 0);
           }
           mma_commit(smem_u32(&bars.empty[s]));
           mma_commit(smem_u32(&bars.pv_done));
-          if (++s == kStages) { s = 0; phase ^= 1u; }
+          if (++s == n_stages) { s = 0; phase ^= 1u; }
         }
         mma_commit(smem_u32(&bars.o_done));
       }
@@ -349,7 +377,8 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done), (g - 1) & 1, kTimeoutMmaDone, abort)))
             break;
           tc_fence_after();
-          for (int c = 0; c < p.dh / 32; ++c) {
+#pragma unroll 1
+          for (int c = 0; c < kDh / 32; ++c) {
             uint32_t o[32];
             tmem_ld32(t_row + kOCol + c * 32, o);
             tmem_ld_wait();
@@ -359,11 +388,11 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
           }
           if (kTcSum) {  // the row-sum columns scale with O
             uint32_t o[16];
-            tmem_ld16(t_row + kOCol + p.dh, o);
+            tmem_ld16(t_row + kOCol + kDh, o);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st16(t_row + kOCol + p.dh, o);
+            tmem_st16(t_row + kOCol + kDh, o);
           }
           tmem_st_wait();
           weights(-m_run);  // lanes whose maximum did not move recompute the same weights
@@ -383,13 +412,14 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       float l_tot = l_run;
       if (kTcSum) {
         uint32_t lr[16];
-        tmem_ld16(t_row + kOCol + p.dh, lr);
+        tmem_ld16(t_row + kOCol + kDh, lr);
         tmem_ld_wait();
         l_tot = __uint_as_float(lr[0]);
       }
       const float inv = 1.f / l_tot;
       __nv_bfloat16* dst = p.out + (static_cast<size_t>(wi.b) * p.n_latent + grow) * p.ld + wi.col0;
-      for (int c = 0; c < p.dh / 32; ++c) {
+#pragma unroll 1
+      for (int c = 0; c < kDh / 32; ++c) {
         uint32_t o[32];
         tmem_ld32(t_row + kOCol + c * 32, o);
         tmem_ld_wait();

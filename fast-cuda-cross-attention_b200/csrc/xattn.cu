@@ -81,11 +81,13 @@ int prepare_device(int* dev_out) {
         cudaFuncSetAttribute(accurate::gemm3x_kernel<true>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, accurate::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
-    if (cudaFuncSetAttribute(mha::mha_bf16_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, mha::kSmemBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(mha::mha_bf16_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, mha::kSmemBytes) != cudaSuccess)
-      return XATTN_ERR_LAUNCH;
+    for (const void* fn : {reinterpret_cast<const void*>(mha::mha_bf16_kernel<32>),
+                           reinterpret_cast<const void*>(mha::mha_bf16_kernel<64>),
+                           reinterpret_cast<const void*>(mha::mha_bf16_kernel<96>),
+                           reinterpret_cast<const void*>(mha::mha_bf16_kernel<128>)})
+      if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, mha::kSmemBytes) !=
+          cudaSuccess)
+        return XATTN_ERR_LAUNCH;
     st.init = true;
   }
   const int want = g_opt_wait_us.load();
@@ -706,8 +708,9 @@ extern "C" int xattn_lse_finalize(const float* ol, float* output, long long rows
 
 // Multi-head bf16 tensor-core kernel (mha_bf16.cuh): heads side by side in rows of
 // heads * head_dim elements.  Persistent: two CTAs per SM (the kernel's occupancy) loop
-// over the B * heads * row-block items.
-int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+// over the B * heads * row-block items.  One instantiation per head dimension.
+template <int kDh>
+int launch_mha_bf16_dh(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
                     __nv_bfloat16* out, int B, int Nl, int Ni, int heads, int dh, int sms,
                     cudaStream_t stream) {
   mha::Params p;
@@ -716,14 +719,13 @@ int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_b
   const uint64_t sq[2] = {ld * 2, (uint64_t)Nl * ld * 2};
   const uint64_t dk[3] = {ld, (uint64_t)Ni, (uint64_t)B};
   const uint64_t sk[2] = {ld * 2, (uint64_t)Ni * ld * 2};
-  const uint32_t bq[3] = {mha::kBoxCols, mha::kRows, 1};
-  const uint32_t bk[3] = {mha::kBoxCols, mha::kKeys, 1};
-  if (!encode_tmap(&p.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, Q, dq, sq, bq,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap(&p.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, K, dk, sk, bk,
-                   CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dk, sk, bk,
-                   CU_TENSOR_MAP_SWIZZLE_128B))
+  using L = mha::Layout<kDh>;
+  const CUtensorMapSwizzle swz = L::kRowB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  const uint32_t bq[3] = {static_cast<uint32_t>(L::kBc), mha::kRows, 1};
+  const uint32_t bk[3] = {static_cast<uint32_t>(L::kBc), mha::kKeys, 1};
+  if (!encode_tmap(&p.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, Q, dq, sq, bq, swz) ||
+      !encode_tmap(&p.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, K, dk, sk, bk, swz) ||
+      !encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dk, sk, bk, swz))
     return XATTN_ERR_ARG;
   p.out = out;
   p.heads = heads;
@@ -737,11 +739,20 @@ int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_b
   if (items > 0x7fffffffLL) return XATTN_ERR_ARG;
   p.n_items = static_cast<int>(items);
   const long long ctas = std::min<long long>(items, 2LL * sms);
-  if (mha::tc_sum_for(dh))
-    mha::mha_bf16_kernel<true><<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
-  else
-    mha::mha_bf16_kernel<false><<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
+  mha::mha_bf16_kernel<kDh><<<static_cast<unsigned>(ctas), mha::kThreads, mha::kSmemBytes, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+int launch_mha_bf16(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __nv_bfloat16* V,
+                    __nv_bfloat16* out, int B, int Nl, int Ni, int heads, int dh, int sms,
+                    cudaStream_t stream) {
+  switch (dh) {
+    case 32: return launch_mha_bf16_dh<32>(Q, K, V, out, B, Nl, Ni, heads, dh, sms, stream);
+    case 64: return launch_mha_bf16_dh<64>(Q, K, V, out, B, Nl, Ni, heads, dh, sms, stream);
+    case 96: return launch_mha_bf16_dh<96>(Q, K, V, out, B, Nl, Ni, heads, dh, sms, stream);
+    case 128: return launch_mha_bf16_dh<128>(Q, K, V, out, B, Nl, Ni, heads, dh, sms, stream);
+    default: return XATTN_ERR_ARG;  // callers check mha::supports_dh first
+  }
 }
 
 extern "C" int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K,

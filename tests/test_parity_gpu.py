@@ -445,7 +445,7 @@ def _bf16_heads_ref(torch, q, k, v, h):
     return ref_attention(torch, heads(q, nl), heads(k, ni), heads(v, ni)).permute(0, 2, 1, 3).reshape(b, nl, dm)
 
 
-@pytest.mark.parametrize("dh", [64, 96, 128])
+@pytest.mark.parametrize("dh", [32, 64, 96, 128])
 def test_bf16_rescale_every_tile(X, torch_cuda, dh):
     """Logits that grow tile by tile (later keys have larger norms) make the running maximum
     jump past the lazy-rescale threshold on every key tile, exercising the O rescale."""
@@ -462,9 +462,12 @@ def test_bf16_rescale_every_tile(X, torch_cuda, dh):
     assert X.device_status() == 0
 
 
-def test_bf16_tensor_core_and_generic_kernels_agree(X, torch_cuda):
+@pytest.mark.parametrize("dh", [32, 64, 96, 128])
+def test_bf16_tensor_core_and_generic_kernels_agree(X, torch_cuda, dh):
+    """Every head dimension the tensor-core kernel takes (64- and 32-column operand boxes)
+    against the generic kernel and the fp32 reference."""
     torch = torch_cuda
-    b, nl, ni, h, dh = 2, 200, 333, 8, 96
+    b, nl, ni, h = 2, 200, 333, 8
     gen = torch.Generator(device="cuda").manual_seed(10)
     q, k, v = (torch.randn(b, n, h * dh, device="cuda", generator=gen).bfloat16() for n in (nl, ni, ni))
     fast = X.cross_attention_bf16_mha(q, k, v, h)
