@@ -21,8 +21,8 @@
 // Operands in shared memory, in boxes of bc columns: bc = 64 (128-byte swizzle rows) for
 // d >= 64, bc = 32 (64-byte swizzle rows) for d = 32.  At d = 96 the second box also holds
 // 32 columns of the next head (or zero fill past the last head) that the MMAs never read:
-// three 32-column boxes would move a quarter fewer bytes, but measured 20 % slower (the
-// tensor core's operand reads from 64-byte swizzle rows cost more than the bytes saved).
+// three 32-column boxes (64-byte swizzle, a 7-stage ring) move a quarter fewer bytes but
+// measured 1 % slower at C5, so the operand stream is not what bounds this kernel.
 //   Q   K-major, dh/bc boxes of 128 rows x bc columns
 //   K   K-major, boxes of 64 keys x bc columns
 //   V   MN-major (rows are keys): the same boxes; the descriptor walks keys in 8-row groups
