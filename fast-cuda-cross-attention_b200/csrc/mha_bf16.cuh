@@ -17,18 +17,22 @@
 //               through a ring in the order K(0), then per tile K(j+1), V(j)
 //   warp 1      MMA issuer: S = Q K^T (M=128, N=64, K=dh), O += P V (M=128, N=dh, K=64)
 //   warps 2..5  softmax, one query row per thread (warp w reads TMEM lanes 32*(w%4)..+31),
-//               then the epilogue
-// Operands in shared memory, in boxes of bc columns: bc = 64 (128-byte swizzle rows) for
-// d >= 64, bc = 32 (64-byte swizzle rows) for d = 32.  At d = 96 the second box also holds
-// 32 columns of the next head (or zero fill past the last head) that the MMAs never read:
-// three 32-column boxes (64-byte swizzle, a 7-stage ring) move a quarter fewer bytes but
-// measured 1 % slower at C5, so the operand stream is not what bounds this kernel.
+//               then the epilogue: O / l in bf16 through per-warp staging slots in shared
+//               memory, written out by TMA stores (32 x 32 boxes) that run while the warps
+//               start the next item; stores of one row per thread took ~1.8 us per item
+// Persistent: two CTAs per SM loop over the (batch, head, 128-row block) items, keeping TMEM,
+// barriers and the ring across items; the next item's Q load and first Q K^T overlap the
+// current item's epilogue.
+// Operands in shared memory, in boxes of bc columns: bc = 64 (128-byte swizzle rows) when d
+// is a multiple of 64, else bc = 32 (64-byte swizzle rows), so every box lies inside the
+// head.  (At d = 96, two 64-column boxes with the next head's columns unused measured 1 %
+// faster at equal ring depth, but leave no room for the output staging.)
 //   Q   K-major, dh/bc boxes of 128 rows x bc columns
 //   K   K-major, boxes of 64 keys x bc columns
 //   V   MN-major (rows are keys): the same boxes; the descriptor walks keys in 8-row groups
 //       (SBO = 8 rows) and head columns in bc-wide groups (LBO = one box)
-// Q and the ring share a 112 KB operand area; the ring takes as many stages as fit (five at
-// d = 96 and 128, kMaxStages at d = 32 and 64).  The barriers live after it: with no static
+// Q, the ring and the output staging share a 112 KB operand area; the ring takes as many
+// stages as fit (four at d = 128, five at d = 96, kMaxStages at d = 32 and 64).  The barriers live after it: with no static
 // shared memory the dynamic region starts 1024-byte aligned (checked at run time), which
 // leaves room for two CTAs per SM.
 // Row sums on the tensor core (kTcSum, d <= 112): with each P.V step the MMA issuer also
@@ -63,7 +67,7 @@ constexpr float kRescaleLog2 = 8.f;  // lazy rescale threshold (log2 units), as 
 
 struct Params {
   CUtensorMap tq, tk, tv;  // boxes of Layout<dh>::kBc columns x (128 or kKeys) rows
-  __nv_bfloat16* out;
+  CUtensorMap to;          // output, boxes of 32 columns x 32 rows, 64-byte swizzle
   int heads, n_latent, n_input, dh, ld;  // ld = heads * dh elements per row
   int n_row_blocks;
   int n_items;                           // B * heads * n_row_blocks
@@ -97,6 +101,12 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&v);
@@ -109,7 +119,7 @@ __host__ __device__ constexpr bool tc_sum_for(int dh) { return dh <= 112; }
 template <int kDh>
 struct Layout {
   static constexpr bool kTcSum = tc_sum_for(kDh);
-  static constexpr int kBc = kDh >= 64 ? 64 : 32;            // columns per box
+  static constexpr int kBc = kDh % 64 == 0 ? 64 : 32;        // columns per box
   static constexpr int kRowB = 2 * kBc;                      // bytes per swizzle row
   static constexpr uint32_t kSwz = kRowB == 128 ? kSw128 : kSw64;
   static constexpr int kBoxes = (kDh + kBc - 1) / kBc;
@@ -117,9 +127,18 @@ struct Layout {
   static constexpr int kKvBox = kKeys * kRowB;
   static constexpr int kStageBytes = kBoxes * kKvBox;
   static constexpr int kQBytes = kBoxes * kQBox;
-  static constexpr int kStages = (kOperandBytes - kQBytes) / kStageBytes < kMaxStages
-                                     ? (kOperandBytes - kQBytes) / kStageBytes
+  // Output staging: per softmax warp, slots of 32 rows x 32 columns (2 KB) for the TMA
+  // store; a slot per 32-column chunk when the ring still keeps 5 stages, else two.
+  static constexpr int kChunks = kDh / 32;
+  static constexpr int kChunkBytes = 32 * 64;
+  static constexpr int kSlots =
+      (kOperandBytes - kQBytes - kSoftmaxWarps * kChunks * kChunkBytes) / kStageBytes >= 5 ? kChunks : 2;
+  static constexpr int kStagingBytes = kSoftmaxWarps * kSlots * kChunkBytes;
+  static constexpr int kStages = (kOperandBytes - kQBytes - kStagingBytes) / kStageBytes < kMaxStages
+                                     ? (kOperandBytes - kQBytes - kStagingBytes) / kStageBytes
                                      : kMaxStages;
+  static constexpr int kStagingOffset = kQBytes + kStages * kStageBytes;
+  static_assert(kStagingOffset + kStagingBytes <= kOperandBytes, "operand area overflow");
   static constexpr int kKStepsBox = kBc / 16;                // K steps of 16 per swizzle row
   static_assert(kStages >= 2, "K/V ring needs two stages");
 };
@@ -141,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   constexpr int stage_bytes = L::kStageBytes, n_stages = L::kStages;
   constexpr uint32_t swz = L::kSwz;
   uint8_t* stages = smem + L::kQBytes;
+  const uint32_t staging = smem_u32(smem + L::kStagingOffset);
   Barriers& bars = *reinterpret_cast<Barriers*>(smem + kBarOffset);
   uint32_t& tmem_slot = bars.tmem_slot;
   int& abort_flag = bars.abort_flag;
@@ -186,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
     tma_prefetch_desc(&p.tq);
     tma_prefetch_desc(&p.tk);
     tma_prefetch_desc(&p.tv);
+    tma_prefetch_desc(&p.to);
   }
   tc_fence_before();
   __syncthreads();
@@ -296,7 +317,6 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
   } else {
     // ============================================================== softmax + epilogue
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     bool ok = true;
     int it = 0;
@@ -404,11 +424,13 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&bars.p_full[sbuf]));
       }
-      // ---- epilogue: O / l -> bf16; reading O precedes the next item's first P V, which
-      // waits for this warp's next p_full arrival
+      // ---- epilogue: O / l -> bf16 -> this warp's staging slots (32 rows x 32 columns, rows
+      // of 64 bytes in the 64-byte swizzle: 16-byte chunk k of row r at k ^ ((r >> 1) & 3),
+      // bank-conflict free) -> one TMA store per chunk, which clips rows past N_latent and
+      // runs while the warp goes on to the next item.  Reading O precedes the next item's
+      // first P V, which waits for this warp's next p_full arrival.
       if (!ok || !(ok = warp_mbar_wait(smem_u32(&bars.o_done), it & 1, kTimeoutMmaDone, abort))) break;
       tc_fence_after();
-      const int grow = wi.row0 + row;
       float l_tot = l_run;
       if (kTcSum) {
         uint32_t lr[16];
@@ -417,25 +439,38 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
         l_tot = __uint_as_float(lr[0]);
       }
       const float inv = 1.f / l_tot;
-      __nv_bfloat16* dst = p.out + (static_cast<size_t>(wi.b) * p.n_latent + grow) * p.ld + wi.col0;
+      const int y0 = wi.row0 + quad * 32;  // this warp's first output row
+      const bool rows_in = y0 < p.n_latent;
+      if (lane == 0) bulk_wait_group_read<0>();  // the previous item's stores read their slots
+      __syncwarp();
 #pragma unroll 1
-      for (int c = 0; c < kDh / 32; ++c) {
+      for (int c = 0; c < L::kChunks; ++c) {
+        const int slot = c % L::kSlots;
+        if (c >= L::kSlots) {  // slot reuse within the item: the store of chunk c - kSlots
+          if (lane == 0) bulk_wait_group_read<L::kSlots - 1>();
+          __syncwarp();
+        }
         uint32_t o[32];
         tmem_ld32(t_row + kOCol + c * 32, o);
         tmem_ld_wait();
-        if (grow < p.n_latent) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+        const uint32_t sbase = staging + (quad * L::kSlots + slot) * L::kChunkBytes;
 #pragma unroll
-          for (int i = 0; i < 4; ++i)
-            d4[i] = make_uint4(
-                pack_bf16x2(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv),
-                pack_bf16x2(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv),
-                pack_bf16x2(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv),
-                pack_bf16x2(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv));
+        for (int k = 0; k < 4; ++k)
+          st_shared_v4(sbase + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4),
+                       pack_bf16x2(__uint_as_float(o[8 * k + 0]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
+                       pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
+                       pack_bf16x2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
+                       pack_bf16x2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && rows_in) {
+          tma_store_3d(&p.to, sbase, wi.col0 + c * 32, y0, wi.b);
+          bulk_commit_group();
         }
       }
       tc_fence_before();
     }
+    if (lane == 0) bulk_wait_group_all();  // stores done before the CTA's shared memory goes
   }
 
   tc_fence_before();

@@ -723,11 +723,13 @@ int launch_mha_bf16_dh(const __nv_bfloat16* Q, const __nv_bfloat16* K, const __n
   const CUtensorMapSwizzle swz = L::kRowB == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
   const uint32_t bq[3] = {static_cast<uint32_t>(L::kBc), mha::kRows, 1};
   const uint32_t bk[3] = {static_cast<uint32_t>(L::kBc), mha::kKeys, 1};
+  const uint32_t bo[3] = {32, 32, 1};  // output chunks of 32 rows x 32 columns
   if (!encode_tmap(&p.tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, Q, dq, sq, bq, swz) ||
       !encode_tmap(&p.tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, K, dk, sk, bk, swz) ||
-      !encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dk, sk, bk, swz))
+      !encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, V, dk, sk, bk, swz) ||
+      !encode_tmap(&p.to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out, dq, sq, bo,
+                   CU_TENSOR_MAP_SWIZZLE_64B))
     return XATTN_ERR_ARG;
-  p.out = out;
   p.heads = heads;
   p.n_latent = Nl;
   p.n_input = Ni;
