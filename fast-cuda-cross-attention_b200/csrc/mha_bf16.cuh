@@ -443,16 +443,20 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       const bool rows_in = y0 < p.n_latent;
       if (lane == 0) bulk_wait_group_read<0>();  // the previous item's stores read their slots
       __syncwarp();
-#pragma unroll 1
+      // chunks in groups of kSlots (one group unless d = 128): the TMEM load of chunk c + 1
+      // is in flight while chunk c is packed; one proxy fence and one bulk group per group
+      uint32_t oa[32], ob[32];
+      tmem_ld32(t_row + kOCol, oa);
+#pragma unroll
       for (int c = 0; c < L::kChunks; ++c) {
         const int slot = c % L::kSlots;
-        if (c >= L::kSlots) {  // slot reuse within the item: the store of chunk c - kSlots
-          if (lane == 0) bulk_wait_group_read<L::kSlots - 1>();
+        if (c >= L::kSlots && slot == 0) {  // group reuses the slots: earlier stores read them
+          if (lane == 0) bulk_wait_group_read<0>();
           __syncwarp();
         }
-        uint32_t o[32];
-        tmem_ld32(t_row + kOCol + c * 32, o);
         tmem_ld_wait();
+        uint32_t* o = (c & 1) ? ob : oa;
+        if (c + 1 < L::kChunks) tmem_ld32(t_row + kOCol + (c + 1) * 32, (c & 1) ? oa : ob);
         const uint32_t sbase = staging + (quad * L::kSlots + slot) * L::kChunkBytes;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -461,11 +465,15 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
                        pack_bf16x2(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
                        pack_bf16x2(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
                        pack_bf16x2(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0 && rows_in) {
-          tma_store_3d(&p.to, sbase, wi.col0 + c * 32, y0, wi.b);
-          bulk_commit_group();
+        if (slot == L::kSlots - 1 || c == L::kChunks - 1) {  // group complete: store it
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && rows_in) {
+            for (int cc = c - slot; cc <= c; ++cc)
+              tma_store_3d(&p.to, staging + (quad * L::kSlots + cc % L::kSlots) * L::kChunkBytes,
+                           wi.col0 + cc * 32, y0, wi.b);
+            bulk_commit_group();
+          }
         }
       }
       tc_fence_before();
