@@ -7,7 +7,9 @@ Functions take CUDA tensors and launch on ``torch.cuda.current_stream()``:
 * ``cross_attention_splitk(q, k, v, num_splits)``  the upstream split-K entry with
   caller-visible (m, l, O) partials (``kernel_splitk.cu:42-251``);
 * ``cross_attention_partial`` / ``combine``        partial triples and their merge;
-* ``cross_attention_bf16_mha(q, k, v, heads)``     multi-head bf16 (no upstream counterpart).
+* ``cross_attention_bf16_mha(q, k, v, heads)``     multi-head bf16 (no upstream counterpart);
+* ``cross_attention_from_host(q, k, v)``  host-resident fp32 inputs and output, batch chunks
+  pipelined through copy-in / compute / copy-out streams.
 
 Multi-GPU (one process per GPU, ``torch.distributed``):
 
@@ -154,6 +156,86 @@ def cross_attention(q, k, v, out=None):
     _raise(lib().xattn_fp32(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni,
                             d, _stream()), "xattn_fp32")
     return out[0] if squeeze else out
+
+
+_COPY_STREAMS = {}
+_HOST_BUFFERS = {}
+
+
+def _copy_streams(dev):
+    """(host->device, device->host) streams of a device, created once."""
+    import torch
+
+    if dev.index not in _COPY_STREAMS:
+        _COPY_STREAMS[dev.index] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return _COPY_STREAMS[dev.index]
+
+
+def cross_attention_from_host(q, k, v, out=None, chunk: Optional[int] = None):
+    """cross_attention for host-resident fp32 q [B,Nl,D], k, v [B,Ni,D]; returns a host tensor.
+
+    The batch is processed in chunks through three CUDA streams: the host->device copy of
+    chunk c+1 and the device->host copy of chunk c-1 run while chunk c computes, on the
+    caller's current stream.  The two copy directions use separate copy engines, so a step
+    costs about its host->device transfer instead of the sum of both transfers and the
+    kernels.  Device buffers persist per device for the last shape used (the output buffer
+    alternates between calls), so the next call's copy-in waits only for this call's last
+    kernel, not for its copy-out.  Inputs should be in pinned memory (otherwise the copies
+    are synchronous and nothing overlaps) and must not change until the caller's stream has
+    passed the call; `out` (host, pinned if given) receives the result.  The call returns
+    once the work is queued, with the caller's stream ordered after the last copy-out.
+    chunk: batches per chunk (default: the batch in 8 chunks).
+    """
+    import torch
+
+    q, k, v = _as3(q), _as3(k), _as3(v)
+    for t in (q, k, v):
+        if t.device.type != "cpu" or t.dtype != torch.float32:
+            raise ValueError("expected float32 host tensors")
+    b = q.shape[0]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    main = torch.cuda.current_stream(dev)
+    s_in, s_out = _copy_streams(dev)
+    if out is None:
+        out = torch.empty(q.shape, dtype=torch.float32, pin_memory=True)
+    chunk = max(1, chunk or (b + 7) // 8)
+    key = (tuple(q.shape), tuple(k.shape))
+    st = _HOST_BUFFERS.get(dev.index)
+    if st is None or st["key"] != key:
+        if st is not None:  # the old buffers are idle before they go back to the allocator
+            main.wait_stream(s_in)
+            main.wait_stream(s_out)
+        st = {"key": key, "dq": torch.empty(q.shape, device=dev), "dk": torch.empty(k.shape, device=dev),
+              "dv": torch.empty(v.shape, device=dev),
+              "do": [torch.empty(q.shape, device=dev), torch.empty(q.shape, device=dev)],
+              "flip": 0, "computed": None}
+        _HOST_BUFFERS[dev.index] = st
+        s_in.wait_stream(main)   # buffers allocated on the caller's stream
+        s_out.wait_stream(main)
+    dq, dk, dv = st["dq"], st["dk"], st["dv"]
+    do = st["do"][st["flip"]]  # the other one may still be copied out by the previous call
+    st["flip"] ^= 1
+    if st["computed"] is not None:
+        s_in.wait_event(st["computed"])  # the previous call's kernels read dq, dk, dv
+    done = None
+    for c0 in range(0, b, chunk):
+        sl = slice(c0, min(b, c0 + chunk))
+        with torch.cuda.stream(s_in):
+            dq[sl].copy_(q[sl], non_blocking=True)
+            dk[sl].copy_(k[sl], non_blocking=True)
+            dv[sl].copy_(v[sl], non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(s_in)
+        main.wait_event(landed)
+        cross_attention(dq[sl], dk[sl], dv[sl], out=do[sl])
+        done = torch.cuda.Event()
+        done.record(main)
+        s_out.wait_event(done)
+        with torch.cuda.stream(s_out):
+            out[sl].copy_(do[sl], non_blocking=True)
+    st["computed"] = done
+    main.wait_stream(s_out)
+    return out
 
 
 def cross_attention_splitk(q, k, v, num_splits: int):
