@@ -77,12 +77,17 @@ constexpr float kRescaleLog2 = 8.0f;        // lazy-rescale threshold (factor 25
 // budget check below together with the dynamic ring + exchange buffer.
 constexpr int kStaticSmemBytes = 1536;
 static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
+// The epilogue stages O in the ring and exchange buffers: 24 KB per softmax warp.
+static_assert(kSoftmaxThreads / 32 * (kMaxDh / 32 / kGroups) * 4096 <= kStages * kStageBytes + kXBufs * kXBytes,
+              "output staging exceeds the operand buffers");
 static_assert(kGroupCols == 64, "two 32-column register halves per softmax thread");
 
 struct Params {
   CUtensorMap tq;   // Q [B][Nl][D] fp32, box {32, 128, 1}, 128B swizzle
   CUtensorMap tk;   // K [B][Ni][D] fp32, box {32, 128, 1}, 128B swizzle
   CUtensorMap tv;   // V [B][Ni][D] fp32, box {32, 16, 1}, 128B swizzle / 32B atoms
+  CUtensorMap to;   // output: out {D, Nl, B} box {32, 32, 1}, or po {D, S, Nl, B} box
+                    // {32, 1, 32, 1} in split mode; 128B swizzle
   float* out;       // [B][Nl][D]                      (final mode)
   float* po;        // [B][Nl][S][D]   unnormalised O  (split mode)
   float* pm;        // [B][Nl][S]      row max of the scaled score, natural-log units
@@ -127,6 +132,60 @@ __device__ __forceinline__ uint32_t x_offset(int chunk, int row) { return (chunk
 // 128 rows x 128 bytes; 16-byte chunk c of row r sits at r*128 + (c ^ (r%8))*16.
 __device__ __forceinline__ uint32_t p_offset(int chunk, int row) {
   return (chunk >> 3) * 16384 + row * 128 + (((chunk & 7) ^ (row & 7)) << 4);
+}
+
+__device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Epilogue store of O (the CTA's dh columns in TMEM, rows of this warp's lane quadrant)
+// through shared memory: the warp's 32-column chunks c = grp, grp + kGroups, .. are scaled
+// and written to its staging boxes (4 KB each: 32 rows of 128 bytes, 16-byte piece k of
+// row r at k ^ (r % 8) -- the TMA 128-byte swizzle, bank-conflict free), then one lane
+// stores them with TMA (boxes of 32 rows x 32 columns, clipped to N_latent) and waits until
+// the boxes have been read, so the staging may be released.  One row per thread with 16-byte
+// global stores took ~12 us per CTA at C3 (each warp store touching 32 rows).
+//   stage_base  this warp's staging (dh / 32 / kGroups boxes of 4 KB)
+//   y0, rows_in the warp's first output row; whether any of its rows exist
+__device__ __forceinline__ void store_o_tma(const CUtensorMap* map, bool split_map, uint32_t stage_base,
+                                            uint32_t t_row, int dh, int grp, int lane, float scale,
+                                            int col0, int split, int y0, int b, bool rows_in) {
+  const int n = (dh / 32 - grp + kGroups - 1) / kGroups;  // chunks of this warp
+  auto put = [&](const uint32_t (&o)[32], int i) {
+    const uint32_t box = stage_base + i * 4096 + lane * 128;
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      st_shared_f4(box + ((k ^ (lane & 7)) << 4), __uint_as_float(o[4 * k]) * scale,
+                   __uint_as_float(o[4 * k + 1]) * scale, __uint_as_float(o[4 * k + 2]) * scale,
+                   __uint_as_float(o[4 * k + 3]) * scale);
+  };
+  uint32_t oa[32], ob[32];  // the TMEM load of the next chunk overlaps the current one's stores
+  if (n > 0) tmem_ld32(t_row + grp * 32, oa);
+  for (int i = 0; i < n; i += 2) {
+    tmem_ld_wait();
+    if (i + 1 < n) tmem_ld32(t_row + (grp + (i + 1) * kGroups) * 32, ob);
+    put(oa, i);
+    if (i + 1 < n) {
+      tmem_ld_wait();
+      if (i + 2 < n) tmem_ld32(t_row + (grp + (i + 2) * kGroups) * 32, oa);
+      put(ob, i + 1);
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && rows_in && n > 0) {
+    for (int i = 0; i < n; ++i) {
+      const int x = col0 + (grp + i * kGroups) * 32;
+      if (split_map)
+        tma_store_4d(map, stage_base + i * 4096, x, split, y0, b);
+      else
+        tma_store_3d(map, stage_base + i * 4096, x, y0, b);
+    }
+    bulk_commit_group();
+    bulk_wait_group_read<0>();
+  }
+  __syncwarp();
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -477,34 +536,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
       tc_fence_after();
       float scale;
-      float* dst;
       if (p.split_mode) {
         // Partials relative to the exact max: O' = O * 2^(m_run - m_true), l' likewise.
         const float f = ex2_approx(m_run - m_true);
         scale = f * p.out_comp;
         const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
-        dst = p.po + pidx * p.dim + col0;
         if (live && h == 0 && grp == 0) {
           p.pm[pidx] = m_true * 0.69314718055994531f;
           p.pl[pidx] = l_tot * f;
         }
       } else {
         scale = p.out_comp / l_tot;
-        dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.dim + col0;
       }
-      for (int c = grp; c < dh / 32; c += kGroups) {
-        uint32_t o[32];
-        tmem_ld32(t_row + c * 32, o);
-        tmem_ld_wait();
-        if (live) {
-          float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(o[4 * i]) * scale, __uint_as_float(o[4 * i + 1]) * scale,
-                                __uint_as_float(o[4 * i + 2]) * scale,
-                                __uint_as_float(o[4 * i + 3]) * scale);
-        }
-      }
+      // every MMA has completed, so the ring and the exchange buffers (the first 224 KB of
+      // dynamic shared memory) are free: 24 KB of staging per softmax warp
+      store_o_tma(&p.to, p.split_mode != 0, smem_u32(smem) + sw * (kMaxDh / 32 / kGroups) * 4096,
+                  t_row, dh, grp, lane, scale, col0, split, row0 + quad * 32, b,
+                  row0 + quad * 32 < p.n_latent);
     } else if (n_tiles == 0 && p.split_mode && live) {
       // Empty split (upstream kernel_splitk.cu:62-71): m = -FLT_MAX, l = 0, O = 0.
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;

@@ -66,6 +66,9 @@ static_assert(kProducers <= kStages, "parity-only empty waits need kProducers <=
 constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
 constexpr int kStaticSmemBytes = 1536;
 static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
+static_assert(kSoftmaxThreads / 32 * (fused::kMaxDh / 32 / kGroups) * 4096 <=
+                  kStages * kStageBytes + kXBufs * kXBytes,
+              "output staging exceeds the operand buffers");
 constexpr int kSoftmaxWarpsPerPair = 2 * kSoftmaxThreads / 32;
 
 // D halves this kernel takes: one pair instruction covers N = dh (dh <= 256) or two of
@@ -479,33 +482,22 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
       tc_fence_after();
       float scale;
-      float* dst;
       if (p.split_mode) {
         const float f = ex2_approx(m_run - m_true);
         scale = f * p.out_comp;
         const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
-        dst = p.po + pidx * p.dim + col0;
         if (live && h == 0 && grp == 0) {
           p.pm[pidx] = m_true * 0.69314718055994531f;
           p.pl[pidx] = l_tot * f;
         }
       } else {
         scale = p.out_comp / l_tot;
-        dst = p.out + (static_cast<size_t>(b) * p.n_latent + grow) * p.dim + col0;
       }
-      for (int c = grp; c < dh / 32; c += kGroups) {
-        uint32_t o[32];
-        tmem_ld32(t_row + c * 32, o);
-        tmem_ld_wait();
-        if (live) {
-          float4* d4 = reinterpret_cast<float4*>(dst + c * 32);
-#pragma unroll
-          for (int i = 0; i < 8; ++i)
-            d4[i] = make_float4(__uint_as_float(o[4 * i]) * scale, __uint_as_float(o[4 * i + 1]) * scale,
-                                __uint_as_float(o[4 * i + 2]) * scale,
-                                __uint_as_float(o[4 * i + 3]) * scale);
-        }
-      }
+      // the pair's MMAs have all completed (o_done is a multicast commit after the last
+      // P.V), so this CTA's ring and exchange buffers are free for the output staging
+      fused::store_o_tma(&p.to, p.split_mode != 0,
+                         smem_u32(smem) + sw * (fused::kMaxDh / 32 / kGroups) * 4096, t_row, dh, grp,
+                         lane, scale, col0, split, row0 + quad * 32, b, row0 + quad * 32 < p.n_latent);
     } else if (n_tiles == 0 && p.split_mode && live) {
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
       float* dst = p.po + pidx * p.dim + col0;

@@ -154,6 +154,25 @@ bool make_fp32_maps(fused::Params& p, const float* Q, const float* K, const floa
                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
 
+// Output map of the fused kernels' TMA-store epilogue: out {D, Nl, B} with boxes of
+// 32 columns x 32 rows, or (split mode) the partials po [B][Nl][S][D] as {D, S, Nl, B} with
+// boxes {32, 1, 32, 1}; rows past N_latent are clipped by the TMA.
+bool make_out_map(fused::Params& p, float* out, float* po, int B, int Nl, int D, int S,
+                  int split_mode) {
+  if (split_mode) {
+    const uint64_t d[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)Nl, (uint64_t)B};
+    const uint64_t st[3] = {(uint64_t)D * 4, (uint64_t)S * D * 4, (uint64_t)Nl * S * D * 4};
+    const uint32_t box[4] = {fused::kChunk, 1, 32, 1};
+    return encode_tmap(&p.to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, po, d, st, box,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  const uint64_t d[3] = {(uint64_t)D, (uint64_t)Nl, (uint64_t)B};
+  const uint64_t st[2] = {(uint64_t)D * 4, (uint64_t)Nl * D * 4};
+  const uint32_t box[3] = {fused::kChunk, 32, 1};
+  return encode_tmap(&p.to, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, d, st, box,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // Score scale and TF32 compensation of a launch.  score_scale < 0 means 1/sqrt(D); exact
 // inputs (already representable in TF32, e.g. widened fp16) take no truncation compensation.
 void set_scale(fused::Params& p, int D, float score_scale, bool exact_inputs) {
@@ -181,6 +200,7 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
       return XATTN_ERR_ARG;
   }
+  if (!make_out_map(p, out, po, B, Nl, D, num_splits, split_mode)) return XATTN_ERR_ARG;
   p.out = out;
   p.po = po;
   p.pm = pm;
@@ -223,6 +243,7 @@ int launch_fused_pair(const float* Q, const float* K, const float* V, float* out
                      CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
       return XATTN_ERR_ARG;
   }
+  if (!make_out_map(p, out, nullptr, B, Nl, D, 1, 0)) return XATTN_ERR_ARG;
   p.out = out;
   p.po = p.pm = p.pl = nullptr;
   p.batch = B;
