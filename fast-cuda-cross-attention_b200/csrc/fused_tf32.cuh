@@ -97,6 +97,7 @@ struct Params {
   int num_splits;    // S (1 in final mode)
   int split_chunk;   // keys per split (upstream rule: ceil(Ni / S))
   int split_mode;    // 0: normalised output, 1: partial triples
+  int n_items;       // work items (persistent kernels loop over them)
   float scale_log2;  // log2(e) / sqrt(D), times the score bias compensation
   float out_comp;    // output bias compensation (1 when off)
 };
@@ -144,21 +145,42 @@ __device__ __forceinline__ void st_shared_f4(uint32_t addr, float a, float b, fl
 // and written to its staging boxes (4 KB each: 32 rows of 128 bytes, 16-byte piece k of
 // row r at k ^ (r % 8) -- the TMA 128-byte swizzle, bank-conflict free), then one lane
 // stores them with TMA (boxes of 32 rows x 32 columns, clipped to N_latent) and waits until
-// the boxes have been read, so the staging may be released.  One row per thread with 16-byte
-// global stores took ~12 us per CTA at C3 (each warp store touching 32 rows).
-//   stage_base  this warp's staging (dh / 32 / kGroups boxes of 4 KB)
+// the boxes have been read, so the staging may be reused.  With fewer staging boxes
+// (box_cap) than chunks this repeats in rounds.  One row per thread with 16-byte global
+// stores took ~12 us per CTA at C3 (each warp store touching 32 rows).
+//   stage_base  this warp's staging (box_cap boxes of 4 KB)
 //   y0, rows_in the warp's first output row; whether any of its rows exist
 __device__ __forceinline__ void store_o_tma(const CUtensorMap* map, bool split_map, uint32_t stage_base,
-                                            uint32_t t_row, int dh, int grp, int lane, float scale,
-                                            int col0, int split, int y0, int b, bool rows_in) {
+                                            int box_cap, uint32_t t_row, int dh, int grp, int lane,
+                                            float scale, int col0, int split, int y0, int b,
+                                            bool rows_in) {
   const int n = (dh / 32 - grp + kGroups - 1) / kGroups;  // chunks of this warp
   auto put = [&](const uint32_t (&o)[32], int i) {
-    const uint32_t box = stage_base + i * 4096 + lane * 128;
+    const uint32_t box = stage_base + (i % box_cap) * 4096 + lane * 128;
 #pragma unroll
     for (int k = 0; k < 8; ++k)
       st_shared_f4(box + ((k ^ (lane & 7)) << 4), __uint_as_float(o[4 * k]) * scale,
                    __uint_as_float(o[4 * k + 1]) * scale, __uint_as_float(o[4 * k + 2]) * scale,
                    __uint_as_float(o[4 * k + 3]) * scale);
+  };
+  int first = 0;  // first chunk of the current round
+  auto flush = [&](int last) {  // store chunks first..last, then free their boxes
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && rows_in) {
+      for (int i = first; i <= last; ++i) {
+        const int x = col0 + (grp + i * kGroups) * 32;
+        const uint32_t box = stage_base + (i % box_cap) * 4096;
+        if (split_map)
+          tma_store_4d(map, box, x, split, y0, b);
+        else
+          tma_store_3d(map, box, x, y0, b);
+      }
+      bulk_commit_group();
+      bulk_wait_group_read<0>();
+    }
+    __syncwarp();
+    first = last + 1;
   };
   uint32_t oa[32], ob[32];  // the TMEM load of the next chunk overlaps the current one's stores
   if (n > 0) tmem_ld32(t_row + grp * 32, oa);
@@ -166,26 +188,14 @@ __device__ __forceinline__ void store_o_tma(const CUtensorMap* map, bool split_m
     tmem_ld_wait();
     if (i + 1 < n) tmem_ld32(t_row + (grp + (i + 1) * kGroups) * 32, ob);
     put(oa, i);
+    if (i == n - 1 || i % box_cap == box_cap - 1) flush(i);
     if (i + 1 < n) {
       tmem_ld_wait();
       if (i + 2 < n) tmem_ld32(t_row + (grp + (i + 2) * kGroups) * 32, oa);
       put(ob, i + 1);
+      if (i + 1 == n - 1 || (i + 1) % box_cap == box_cap - 1) flush(i + 1);
     }
   }
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0 && rows_in && n > 0) {
-    for (int i = 0; i < n; ++i) {
-      const int x = col0 + (grp + i * kGroups) * 32;
-      if (split_map)
-        tma_store_4d(map, stage_base + i * 4096, x, split, y0, b);
-      else
-        tma_store_3d(map, stage_base + i * 4096, x, y0, b);
-    }
-    bulk_commit_group();
-    bulk_wait_group_read<0>();
-  }
-  __syncwarp();
 }
 
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
@@ -551,8 +561,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // every MMA has completed, so the ring and the exchange buffers (the first 224 KB of
       // dynamic shared memory) are free: 24 KB of staging per softmax warp
       store_o_tma(&p.to, p.split_mode != 0, smem_u32(smem) + sw * (kMaxDh / 32 / kGroups) * 4096,
-                  t_row, dh, grp, lane, scale, col0, split, row0 + quad * 32, b,
-                  row0 + quad * 32 < p.n_latent);
+                  kMaxDh / 32 / kGroups, t_row, dh, grp, lane, scale, col0, split, row0 + quad * 32,
+                  b, row0 + quad * 32 < p.n_latent);
     } else if (n_tiles == 0 && p.split_mode && live) {
       // Empty split (upstream kernel_splitk.cu:62-71): m = -FLT_MAX, l = 0, O = 0.
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;

@@ -63,6 +63,7 @@ constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (kProducers - 1);
 // alias an older phase because the producer's previous stage, i + kStages - kProducers,
 // already required stage i - kProducers <= i - kStages to be consumed.
 static_assert(kProducers <= kStages, "parity-only empty waits need kProducers <= kStages");
+static_assert(kXBufs == 2, "the exchange permissions below assume double-buffered exchange");
 constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
 constexpr int kStaticSmemBytes = 1536;
 static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
@@ -83,7 +84,10 @@ struct __align__(8) Barriers {
   uint64_t empty[kStages];  // both: the pair MMA consumed a stage (multicast commit)
   uint64_t s_full;          // both: S tile ready (multicast)
   uint64_t s_free;          // leader: both CTAs copied S out of TMEM
-  uint64_t p_full;          // leader: both CTAs wrote P
+  uint64_t p_full[kXBufs];  // leader: both CTAs wrote P of tile g (barrier g % 2).  One per
+                            // buffer: the pair CTAs are not synchronised between releasing S
+                            // and publishing P, so one CTA may publish tile g+1 before the
+                            // other publishes tile g (never g+2: Q.K^T(g+2) follows P.V(g))
   uint64_t pv_done[kXBufs]; // both: P.V on buffer b complete (multicast)
   uint64_t o_done;          // both: last P.V complete (multicast)
   uint64_t x_full[kXBufs];  // D-peer -> me: partial scores in my buffer b
@@ -113,16 +117,26 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   const uint16_t pair_mask = static_cast<uint16_t>(3u << leader);
   const bool is_leader = (r == 0);
 
-  // ---- work item: (batch, 256-row block, split)
-  const int item = blockIdx.x / 4;
+  // ---- work items: (batch, 256-row block, split); the cluster takes items cid,
+  // cid + n_clusters, ...  Every role walks the same sequence and numbers the key tiles of
+  // its items globally (g): the per-tile barriers' phases follow g, o_done's the item count.
+  const int cid = blockIdx.x / 4;
+  const int n_clusters = gridDim.x / 4;
   const int n_rb2 = (p.n_latent + 2 * kRows - 1) / (2 * kRows);
-  const int split = item % p.num_splits;
-  const int rb2 = (item / p.num_splits) % n_rb2;
-  const int b = item / (p.num_splits * n_rb2);
-  const int row0 = rb2 * 2 * kRows + static_cast<int>(r) * kRows;  // this CTA's rows
-  const int k_begin = split * p.split_chunk;
-  const int k_end = min(k_begin + p.split_chunk, p.n_input);
-  const int n_tiles = k_end > k_begin ? (k_end - k_begin + kKeys - 1) / kKeys : 0;
+  struct Item {
+    int b, split, row0, k_begin, k_end, n_tiles;
+  };
+  auto item_at = [&](int item) {
+    Item w;
+    w.split = item % p.num_splits;
+    const int rb2 = (item / p.num_splits) % n_rb2;
+    w.b = item / (p.num_splits * n_rb2);
+    w.row0 = rb2 * 2 * kRows + static_cast<int>(r) * kRows;  // this CTA's rows
+    w.k_begin = w.split * p.split_chunk;
+    w.k_end = min(w.k_begin + p.split_chunk, p.n_input);
+    w.n_tiles = w.k_end > w.k_begin ? (w.k_end - w.k_begin + kKeys - 1) / kKeys : 0;
+    return w;
+  };
   const int dh = p.dh;
   const int n_qk_chunks = dh / kChunk;
   const int col0 = static_cast<int>(h) * dh;
@@ -140,7 +154,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     }
     mbar_init(smem_u32(&bars.s_full), 1);
     mbar_init(smem_u32(&bars.s_free), kSoftmaxWarpsPerPair);
-    mbar_init(smem_u32(&bars.p_full), kSoftmaxWarpsPerPair);
+    for (int i = 0; i < kXBufs; ++i) mbar_init(smem_u32(&bars.p_full[i]), kSoftmaxWarpsPerPair);
     for (int i = 0; i < kXBufs; ++i) {
       mbar_init(smem_u32(&bars.pv_done[i]), 1);
       mbar_init(smem_u32(&bars.x_full[i]), 1);
@@ -174,9 +188,9 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     // from i alone.  One issuing warp sustains only a few million copies per second, well
     // short of what the MMAs consume; several issuing warps multiply that rate.
     const int pid = warp == 0 ? 0 : warp - kFirstExtraProducer + 1;
-    if (elect_one() && n_tiles > 0) {
+    if (elect_one()) {
       bool ok = true;
-      int i = 0;  // stage index in the sequence
+      int i = 0;  // stage index in the sequence (continues across items)
       // True if this producer owns stage i and its slot is free; `fb` is then the leader's
       // full barrier of the slot (cluster address), armed for both CTAs' bytes.
       uint32_t fb = 0;
@@ -191,51 +205,55 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         fb = mapa_shared(smem_u32(&bars.full[slot]), leader);
         return true;
       };
-      auto load_qk = [&](int j) {
-        const int key0 = k_begin + j * kKeys;
-        const int valid = min(kKeys, k_end - key0);
-        const int n_qk = (valid + 15) & ~15;
-        const int kbase = key0 + static_cast<int>(r) * (n_qk / 2);  // this CTA's half of the keys
-        if (pid == 0) {
-          XATTN_TRACE_POINT(0, j);
-          // warm L2 with this tile's V, loaded about one tile from now (a quarter of the
-          // operand reads otherwise miss the near L2 partition)
-          for (int v = 0; v * kVKeys < valid; ++v)
-            for (int n = 0; n < n_instr; ++n)
-              tma_prefetch_4d(&p.tv, 0, key0 + v * kVKeys,
-                              (col0 + n * nn + static_cast<int>(r) * (nn / 2)) / kChunk, b);
-        }
-        for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
-          if (!own(16384 + 8192)) continue;
-          const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
-          tma_load_3d_pair(st, &p.tq, fb, col0 + c * kChunk, row0, b);
-          tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * kChunk, kbase, b);
-          // and the same chunk of the next tile's keys (out-of-range boxes prefetch nothing)
-          if (j + 1 < n_tiles)
-            tma_prefetch_3d(&p.tk, col0 + c * kChunk, key0 + kKeys + static_cast<int>(r) * (kKeys / 2), b);
-        }
-      };
-      auto load_v = [&](int j) {
-        const int key0 = k_begin + j * kKeys;
-        const int valid = min(kKeys, k_end - key0);
-        const int n_v = (valid + kVKeys - 1) / kVKeys;
-        if (pid == 0) XATTN_TRACE_POINT(1, j);
-        for (int v = 0; v < n_v && ok; ++v, ++i) {
-          if (!own(n_slabs * kVKeys * 128)) continue;
-          const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
-          // one box of spi 32-column slabs per instruction: slab index (dim / 32) is the
-          // tensor map's third coordinate
-          for (int n = 0; n < n_instr; ++n) {
-            const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2);
-            tma_load_4d_pair(st + n * spi * (kVKeys * 128), &p.tv, fb, 0, key0 + v * kVKeys,
-                             dim / kChunk, b);
+      for (int item = cid; item < p.n_items && ok; item += n_clusters) {
+        const Item w = item_at(item);
+        auto load_qk = [&](int j) {
+          const int key0 = w.k_begin + j * kKeys;
+          const int valid = min(kKeys, w.k_end - key0);
+          const int n_qk = (valid + 15) & ~15;
+          const int kbase = key0 + static_cast<int>(r) * (n_qk / 2);  // this CTA's half of the keys
+          if (pid == 0) {
+            XATTN_TRACE_POINT(0, j);
+            // warm L2 with this tile's V, loaded about one tile from now (a quarter of the
+            // operand reads otherwise miss the near L2 partition)
+            for (int v = 0; v * kVKeys < valid; ++v)
+              for (int n = 0; n < n_instr; ++n)
+                tma_prefetch_4d(&p.tv, 0, key0 + v * kVKeys,
+                                (col0 + n * nn + static_cast<int>(r) * (nn / 2)) / kChunk, w.b);
           }
+          for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
+            if (!own(16384 + 8192)) continue;
+            const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
+            tma_load_3d_pair(st, &p.tq, fb, col0 + c * kChunk, w.row0, w.b);
+            tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * kChunk, kbase, w.b);
+            // and the same chunk of the next tile's keys (out-of-range boxes prefetch nothing)
+            if (j + 1 < w.n_tiles)
+              tma_prefetch_3d(&p.tk, col0 + c * kChunk, key0 + kKeys + static_cast<int>(r) * (kKeys / 2), w.b);
+          }
+        };
+        auto load_v = [&](int j) {
+          const int key0 = w.k_begin + j * kKeys;
+          const int valid = min(kKeys, w.k_end - key0);
+          const int n_v = (valid + kVKeys - 1) / kVKeys;
+          if (pid == 0) XATTN_TRACE_POINT(1, j);
+          for (int v = 0; v < n_v && ok; ++v, ++i) {
+            if (!own(n_slabs * kVKeys * 128)) continue;
+            const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
+            // one box of spi 32-column slabs per instruction: slab index (dim / 32) is the
+            // tensor map's third coordinate
+            for (int n = 0; n < n_instr; ++n) {
+              const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2);
+              tma_load_4d_pair(st + n * spi * (kVKeys * 128), &p.tv, fb, 0, key0 + v * kVKeys,
+                               dim / kChunk, w.b);
+            }
+          }
+        };
+        if (w.n_tiles == 0) continue;
+        load_qk(0);
+        for (int j = 0; j < w.n_tiles && ok; ++j) {
+          if (j + 1 < w.n_tiles) load_qk(j + 1);
+          load_v(j);
         }
-      };
-      load_qk(0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles) load_qk(j + 1);
-        load_v(j);
       }
       // Drain (producer 0): the pair MMA releases every stage it consumed; wait for the last
       // use of every slot so no load into this CTA's shared memory is still in flight at exit.
@@ -248,14 +266,17 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ================================================================ MMA issuer (pair leader)
     if (is_leader && elect_one()) {
-      if (n_tiles > 0) {
-        int s = 0;
-        uint32_t phase = 0;
-        bool ok = true;
-        const uint32_t t_s = tmem + kSCol;
+      int s = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int g = 0;  // global index of the item's first tile
+      const uint32_t t_s = tmem + kSCol;
+      for (int item = cid; item < p.n_items && ok; item += n_clusters) {
+        const Item w = item_at(item);
+        if (w.n_tiles == 0) continue;
         auto mma_qk = [&](int j) {
-          const int key0 = k_begin + j * kKeys;
-          const int valid = min(kKeys, k_end - key0);
+          const int key0 = w.k_begin + j * kKeys;
+          const int valid = min(kKeys, w.k_end - key0);
           const int n_qk = (valid + 15) & ~15;
           const uint32_t idesc = instr_desc(2, 2 * kRows, n_qk, false, false);
           for (int c = 0; c < n_qk_chunks && ok; ++c) {
@@ -275,21 +296,32 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           if (ok) mma_commit_pair_mc(smem_u32(&bars.s_full), pair_mask);
           XATTN_TRACE_POINT(3, j);
         };
+        // S is single-buffered: the item's first Q.K^T waits until the softmax warps copied
+        // the previous item's last S out of TMEM.  (Its first P.V, which overwrites O, waits
+        // for P, which the softmax warps publish only after the previous epilogue read O.)
+        if (g > 0) {
+          if (!(ok = mbar_wait<true>(smem_u32(&bars.s_free), (g - 1) & 1, kTimeoutSoftmax, abort)))
+            break;
+          tc_fence_after();
+        }
         mma_qk(0);
-        for (int j = 0; j < n_tiles && ok; ++j) {
-          if (j + 1 < n_tiles) {
-            if (!(ok = mbar_wait<true>(smem_u32(&bars.s_free), j & 1, kTimeoutSoftmax, abort))) break;
+        for (int j = 0; j < w.n_tiles && ok; ++j) {
+          const int gj = g + j;
+          if (j + 1 < w.n_tiles) {
+            if (!(ok = mbar_wait<true>(smem_u32(&bars.s_free), gj & 1, kTimeoutSoftmax, abort))) break;
             tc_fence_after();
             mma_qk(j + 1);
             if (!ok) break;
           }
-          if (!(ok = mbar_wait<true>(smem_u32(&bars.p_full), j & 1, kTimeoutSoftmax, abort))) break;
+          if (!(ok = mbar_wait<true>(smem_u32(&bars.p_full[gj % kXBufs]), (gj / kXBufs) & 1,
+                                     kTimeoutSoftmax, abort)))
+            break;
           XATTN_TRACE_POINT(4, j);
           tc_fence_after();
-          const int key0 = k_begin + j * kKeys;
-          const int valid = min(kKeys, k_end - key0);
+          const int key0 = w.k_begin + j * kKeys;
+          const int valid = min(kKeys, w.k_end - key0);
           const int n_v = (valid + kVKeys - 1) / kVKeys;
-          const uint32_t xb = smem_u32(xbuf + (j % kXBufs) * kXBytes);
+          const uint32_t xb = smem_u32(xbuf + (gj % kXBufs) * kXBytes);
           const uint32_t idesc_pv = instr_desc(2, 2 * kRows, nn, false, true);
           for (int v = 0; v < n_v; ++v) {
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
@@ -309,10 +341,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             if (++s == kStages) { s = 0; phase ^= 1u; }
           }
           if (!ok) break;
-          mma_commit_pair_mc(smem_u32(&bars.pv_done[j % kXBufs]), pair_mask);
+          mma_commit_pair_mc(smem_u32(&bars.pv_done[gj % kXBufs]), pair_mask);
           XATTN_TRACE_POINT(5, j);
         }
+        if (!ok) break;
         mma_commit_pair_mc(smem_u32(&bars.o_done), pair_mask);
+        g += w.n_tiles;
       }
       mma_commit_pair_mc(smem_u32(&bars.drain), static_cast<uint16_t>(1u << rank));
       mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, nullptr);
@@ -331,26 +365,32 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t peer_x_full0 = mapa_shared(smem_u32(&bars.x_full[0]), dpeer);
     const uint32_t peer_x_empty = mapa_shared(smem_u32(&bars.x_empty), dpeer);
     const uint32_t lead_s_free = mapa_shared(smem_u32(&bars.s_free), leader);
-    const uint32_t lead_p_full = mapa_shared(smem_u32(&bars.p_full), leader);
+    const uint32_t lead_p_full0 = mapa_shared(smem_u32(&bars.p_full[0]), leader);
     const bool arm_thread = (sw == 0 && lane == 0);
 
-    float m_run = -INFINITY;
-    float m_true = -INFINITY;
-    float l_run = 0.f;
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      const int key0 = k_begin + j * kKeys;
-      const int valid = min(kKeys, k_end - key0);
-      // buffer of tile j: j % kXBufs, used for the (j / kXBufs)-th time
-      const int xb_i = j % kXBufs;
-      const uint32_t xb_par = static_cast<uint32_t>(j / kXBufs) & 1u;
+    int g = 0;   // global index of the item's first tile
+    int it = 0;  // items with tiles done
+    for (int item = cid; item < p.n_items; item += n_clusters) {
+      const Item w = item_at(item);
+      const int b = w.b, split = w.split, row0 = w.row0;
+      float m_run = -INFINITY;
+      float m_true = -INFINITY;
+      float l_run = 0.f;
+    for (int j = 0; j < w.n_tiles; ++j) {
+      const int gj = g + j;  // global tile index
+      const int key0 = w.k_begin + j * kKeys;
+      const int valid = min(kKeys, w.k_end - key0);
+      // buffer of tile gj: gj % kXBufs, used for the (gj / kXBufs)-th time
+      const int xb_i = gj % kXBufs;
+      const uint32_t xb_par = static_cast<uint32_t>(gj / kXBufs) & 1u;
       uint8_t* xcur = xbuf + xb_i * kXBytes;
       const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
       const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
       // After a failed bounded wait a warp keeps iterating with the work skipped (later waits
       // fail at once through the abort flag), so every softmax warp reaches each named
       // barrier equally often and none is left in bar.sync.
-      ok = ok && warp_mbar_wait(smem_u32(&bars.s_full), j & 1, kTimeoutMmaDone, abort);
+      ok = ok && warp_mbar_wait(smem_u32(&bars.s_full), gj & 1, kTimeoutMmaDone, abort);
       uint32_t ra[32], rb[32];
       float gmax = -INFINITY;
       if (ok) {
@@ -364,15 +404,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_remote(lead_s_free);
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
-        if (kXBufs == 1 && j >= 1) {
-          // single buffer: it held P of tile j-1; free once that P.V completed
-          ok = warp_mbar_wait(smem_u32(&bars.pv_done[0]), (j - 1) & 1, kTimeoutMmaDone, abort);
-          if (ok && sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
-          if (ok && lane == 0) mbar_arrive_remote(peer_x_empty);
-        }
       }
-      if (ok && j >= kXBufs)
-        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (j - kXBufs) & 1, kTimeoutExchange, abort);
+      // the D-peer's buffer gj % 2 is free for this tile once it signalled so (tiles >= 2)
+      if (ok && gj >= kXBufs)
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (gj - kXBufs) & 1, kTimeoutExchange, abort);
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
 #pragma unroll
@@ -410,7 +445,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(9, j);
       float tmax = red[0][row];
 #pragma unroll
-      for (int g = 1; g < kGroups; ++g) tmax = fmaxf(tmax, red[g][row]);
+      for (int gg = 1; gg < kGroups; ++gg) tmax = fmaxf(tmax, red[gg][row]);
       named_bar_sync(2 + quad, 32 * kGroups);
       if (!ok) continue;
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(15, j);
@@ -423,8 +458,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         m_run = tmax;
       }
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j - 1) % kXBufs]),
-                                  static_cast<uint32_t>((j - 1) / kXBufs) & 1u, kTimeoutMmaDone,
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(gj - 1) % kXBufs]),
+                                  static_cast<uint32_t>((gj - 1) / kXBufs) & 1u, kTimeoutMmaDone,
                                   abort)))
           continue;
         tc_fence_after();
@@ -458,28 +493,34 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(17, j);
-      if (lane == 0) mbar_arrive_remote(lead_p_full);
+      if (lane == 0) mbar_arrive_remote(lead_p_full0 + xb_i * 8);
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
-      if (kXBufs == 2 && j >= 1 && j + 1 < n_tiles) {
-        // double buffer: buffer (j+1) % 2 held P of tile j-1; free once that P.V completed
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(j + 1) % kXBufs]),
-                                  static_cast<uint32_t>((j - 1) / kXBufs) & 1u, kTimeoutMmaDone,
+      if (gj >= 1 && j + 1 < w.n_tiles) {
+        // my buffer (gj+1) % 2 held P of tile gj-1; once that P.V completed the D-peer may
+        // send tile gj+1 into it.  Every global tile t >= 2 is released exactly once: here
+        // by the end of tile t-1 of the same item, or after the previous item's epilogue
+        // (which stages the output in these buffers) for an item's first tile.  Consecutive
+        // releases from one warp are separated by the all-warp barrier of a tile, so no
+        // warp's arrival counts toward another release's phase.
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(gj + 1) % kXBufs]),
+                                  static_cast<uint32_t>((gj - 1) / kXBufs) & 1u, kTimeoutMmaDone,
                                   abort)))
           continue;
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
         if (lane == 0) mbar_arrive_remote(peer_x_empty);
       }
     }
-    // ---- epilogue
+    // ---- epilogue of the item
     red[grp][row] = l_run;
     named_bar_sync(2 + quad, 32 * kGroups);
     float l_tot = 0.f;
 #pragma unroll
-    for (int g = 0; g < kGroups; ++g) l_tot += red[g][row];
+    for (int gg = 0; gg < kGroups; ++gg) l_tot += red[gg][row];
+    named_bar_sync(2 + quad, 32 * kGroups);  // red is rewritten by the next tile
     const int grow = row0 + row;
     const bool live = grow < p.n_latent;
-    if (ok && n_tiles > 0 &&
-        warp_mbar_wait(smem_u32(&bars.o_done), 0, kTimeoutMmaDone, abort)) {
+    if (ok && w.n_tiles > 0 &&
+        (ok = warp_mbar_wait(smem_u32(&bars.o_done), it & 1, kTimeoutMmaDone, abort))) {
       tc_fence_after();
       float scale;
       if (p.split_mode) {
@@ -493,12 +534,18 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       } else {
         scale = p.out_comp / l_tot;
       }
-      // the pair's MMAs have all completed (o_done is a multicast commit after the last
-      // P.V), so this CTA's ring and exchange buffers are free for the output staging
-      fused::store_o_tma(&p.to, p.split_mode != 0,
-                         smem_u32(smem) + sw * (fused::kMaxDh / 32 / kGroups) * 4096, t_row, dh, grp,
-                         lane, scale, col0, split, row0 + quad * 32, b, row0 + quad * 32 < p.n_latent);
-    } else if (n_tiles == 0 && p.split_mode && live) {
+      // o_done (a multicast commit after the item's last P.V) means every P.V of the item
+      // completed, so both exchange buffers are free (the ring already holds the next
+      // item's operands): 16 KB of staging per softmax warp, O stored in rounds
+      fused::store_o_tma(&p.to, p.split_mode != 0, smem_u32(xbuf) + sw * (kXBufs * kXBytes / (kSoftmaxThreads / 32)),
+                         kXBufs * kXBytes / (kSoftmaxThreads / 32) / 4096, t_row, dh, grp, lane, scale,
+                         col0, split, row0 + quad * 32, b, row0 + quad * 32 < p.n_latent);
+      tc_fence_before();
+      // the staging has been read: the D-peer may send the next item's first tile into my
+      // buffer (g + n_tiles) % 2, whose last P.V (tile g + n_tiles - 2) is complete
+      if (g + w.n_tiles >= kXBufs && item + n_clusters < p.n_items && lane == 0)
+        mbar_arrive_remote(peer_x_empty);
+    } else if (w.n_tiles == 0 && p.split_mode && live) {
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
       float* dst = p.po + pidx * p.dim + col0;
       for (int c = grp; c < dh; c += kGroups) dst[c] = 0.f;
@@ -506,6 +553,11 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         p.pm[pidx] = -3.4028234663852886e38f;
         p.pl[pidx] = 0.f;
       }
+    }
+    if (w.n_tiles > 0) {
+      g += w.n_tiles;
+      ++it;
+    }
     }
   }
 

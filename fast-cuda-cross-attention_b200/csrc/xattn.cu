@@ -55,6 +55,7 @@ int set_error(int code) {
 struct DeviceState {
   bool init = false;
   int sms = 148;
+  int pair_slots = 0;  // co-resident 4-CTA clusters of the pair kernel (0: unknown)
   int wait_us = -1;  // value last copied into g_wait_ns on this device
 };
 std::mutex g_mu;
@@ -76,6 +77,20 @@ int prepare_device(int* dev_out) {
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pair4::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
+    {
+      // the persistent pair kernel launches one cluster per co-resident slot (33 on a B200:
+      // four-CTA clusters of one CTA per SM cannot use every SM of a GPC)
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(4 * 1024);
+      cfg.blockDim = dim3(pair4::kThreads);
+      cfg.dynamicSmemBytes = pair4::kSmemBytes;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(pair4::fused_tf32_pair_kernel),
+                                         &cfg) == cudaSuccess && n > 0)
+        st.pair_slots = n;
+      else
+        cudaGetLastError();  // unknown: one cluster per item
+    }
     if (cudaFuncSetAttribute(accurate::gemm3x_kernel<false>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize, accurate::kSmemBytes) != cudaSuccess ||
         cudaFuncSetAttribute(accurate::gemm3x_kernel<true>,
@@ -217,6 +232,7 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
   set_scale(p, D, score_scale, exact_inputs);
   const long long items = static_cast<long long>(B) * p.n_row_blocks * num_splits;
   if (items * 2 > 0x7fffffffLL) return XATTN_ERR_ARG;
+  p.n_items = static_cast<int>(items);
   fused::fused_tf32_kernel<<<static_cast<unsigned>(items * 2), fused::kThreads, fused::kSmemBytes,
                              stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
@@ -258,7 +274,13 @@ int launch_fused_pair(const float* Q, const float* K, const float* V, float* out
   set_scale(p, D, score_scale, exact_inputs);
   const long long items = static_cast<long long>(B) * p.n_row_blocks;
   if (items * 4 > 0x7fffffffLL) return XATTN_ERR_ARG;
-  pair4::fused_tf32_pair_kernel<<<static_cast<unsigned>(items * 4), pair4::kThreads,
+  p.n_items = static_cast<int>(items);
+  // persistent: one cluster per co-resident slot, each looping over items
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int slots = dev >= 0 && dev < 64 ? g_dev[dev].pair_slots : 0;
+  const long long clusters = slots > 0 ? std::min<long long>(items, slots) : items;
+  pair4::fused_tf32_pair_kernel<<<static_cast<unsigned>(clusters * 4), pair4::kThreads,
                                   pair4::kSmemBytes, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
