@@ -27,6 +27,8 @@
 // bounded by the 128 KB of exchange / P buffers beside it.
 #pragma once
 
+#include <cuda_fp16.h>
+
 #include "fused_tf32.cuh"
 
 namespace xattn {
@@ -47,7 +49,48 @@ using fused::p_offset;
 using fused::Params;
 using fused::x_offset;
 
-constexpr int kVKeys = 32;           // keys per V chunk (four K=8 steps)
+// Element type of the operands: fp32 (kind::tf32, the fp32 API) or fp16 (kind::f16, the
+// upstream WMMA entries with fp16 inputs).  A 128-byte swizzle row holds kCols elements;
+// Q/K stages and V stages keep their byte sizes, P (the A operand of P.V) is stored in T.
+template <typename T>
+struct Elem;
+template <>
+struct Elem<float> {
+  static constexpr int kCols = 32;                // fp32 per 128-byte swizzle row
+  static constexpr int kVKeys = 32;               // keys per V stage (four K=8 steps)
+  static constexpr int kKStep = 8;                // MMA K per instruction
+  static constexpr uint32_t kFmt = 2;             // instruction descriptor: tf32
+  static constexpr uint32_t kVSwz = kSw128Atom32; // V MN-major: 128-byte swizzle, 32-byte atoms
+  static constexpr uint32_t kVSbo = 512;
+  // P.V instructions per K step (pair N = dh / n <= 256, whole 32-column slabs per CTA)
+  __host__ __device__ static constexpr int n_instr(int dh) { return dh <= 256 ? 1 : 2; }
+  __host__ __device__ static constexpr bool supports(int dh) {
+    return dh == 64 || dh == 128 || dh == 192 || dh == 256 || dh == 384;
+  }
+};
+template <>
+struct Elem<__half> {
+  static constexpr int kCols = 64;                // fp16 per 128-byte swizzle row
+  static constexpr int kVKeys = 64;               // keys per V stage (four K=16 steps)
+  static constexpr int kKStep = 16;
+  static constexpr uint32_t kFmt = 0;             // instruction descriptor: f16
+  static constexpr uint32_t kVSwz = kSw128;       // V MN-major, 128-byte swizzle
+  static constexpr uint32_t kVSbo = 1024;
+  // pair N = 128 per instruction: one 64-column slab per CTA
+  __host__ __device__ static constexpr int n_instr(int dh) { return dh / 128; }
+  __host__ __device__ static constexpr bool supports(int dh) {
+    return dh == 128 || dh == 256 || dh == 384;
+  }
+};
+
+template <typename T>
+__device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                         uint32_t acc) {
+  if constexpr (sizeof(T) == 4)
+    mma_tf32_ss_pair(d, a, b, idesc, acc);
+  else
+    mma_f16_ss_pair(d, a, b, idesc, acc);
+}
 constexpr int kStageBytes = 24576;   // Q chunk 16 KB + K half 8 KB, or a V chunk
 // Exchange / P buffers: 2 (the next tile's exchange overlaps this tile's P.V; 4 stages), or
 // 1 (a 6-stage ring, 144 KB of operands in flight, but the exchange then waits for P.V:
@@ -75,9 +118,7 @@ constexpr int kSoftmaxWarpsPerPair = 2 * kSoftmaxThreads / 32;
 // D halves this kernel takes: one pair instruction covers N = dh (dh <= 256) or two of
 // N = dh / 2 (dh = 384); each CTA holds N / 2 columns of V per instruction, whole 32-wide
 // slabs.
-__host__ __device__ constexpr bool supports_dh(int dh) {
-  return dh == 64 || dh == 128 || dh == 192 || dh == 256 || dh == 384;
-}
+__host__ __device__ constexpr bool supports_dh(int dh) { return Elem<float>::supports(dh); }
 
 struct __align__(8) Barriers {
   uint64_t full[kStages];   // leader: both CTAs' loads of a stage landed
@@ -95,8 +136,11 @@ struct __align__(8) Barriers {
   uint64_t drain;           // leader: its MMAs completed
 };
 
+template <typename T>
 __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     fused_tf32_pair_kernel(const __grid_constant__ Params p) {
+  using E = Elem<T>;
+  constexpr int kVKeys = E::kVKeys;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -138,11 +182,11 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     return w;
   };
   const int dh = p.dh;
-  const int n_qk_chunks = dh / kChunk;
+  const int n_qk_chunks = dh / E::kCols;
   const int col0 = static_cast<int>(h) * dh;
-  const int n_instr = dh <= 256 ? 1 : 2;         // P.V instructions per K step
+  const int n_instr = E::n_instr(dh);            // P.V instructions per K step
   const int nn = dh / n_instr;                    // pair N per instruction
-  const int spi = nn / 64;                        // 32-wide V slabs per CTA per instruction
+  const int spi = nn / (2 * E::kCols);            // V slabs (one swizzle row wide) per CTA per instruction
   const int n_slabs = spi * n_instr;              // V slabs this CTA loads per chunk
 
   if (threadIdx.x == 0) {
@@ -219,16 +263,16 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             for (int v = 0; v * kVKeys < valid; ++v)
               for (int n = 0; n < n_instr; ++n)
                 tma_prefetch_4d(&p.tv, 0, key0 + v * kVKeys,
-                                (col0 + n * nn + static_cast<int>(r) * (nn / 2)) / kChunk, w.b);
+                                (col0 + n * nn + static_cast<int>(r) * (nn / 2)) / E::kCols, w.b);
           }
           for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
             if (!own(16384 + 8192)) continue;
             const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
-            tma_load_3d_pair(st, &p.tq, fb, col0 + c * kChunk, w.row0, w.b);
-            tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * kChunk, kbase, w.b);
+            tma_load_3d_pair(st, &p.tq, fb, col0 + c * E::kCols, w.row0, w.b);
+            tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * E::kCols, kbase, w.b);
             // and the same chunk of the next tile's keys (out-of-range boxes prefetch nothing)
             if (j + 1 < w.n_tiles)
-              tma_prefetch_3d(&p.tk, col0 + c * kChunk, key0 + kKeys + static_cast<int>(r) * (kKeys / 2), w.b);
+              tma_prefetch_3d(&p.tk, col0 + c * E::kCols, key0 + kKeys + static_cast<int>(r) * (kKeys / 2), w.b);
           }
         };
         auto load_v = [&](int j) {
@@ -239,12 +283,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           for (int v = 0; v < n_v && ok; ++v, ++i) {
             if (!own(n_slabs * kVKeys * 128)) continue;
             const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
-            // one box of spi 32-column slabs per instruction: slab index (dim / 32) is the
-            // tensor map's third coordinate
+            // one box of spi slabs per instruction: slab index (dim / kCols) is the tensor
+            // map's third coordinate
             for (int n = 0; n < n_instr; ++n) {
               const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2);
               tma_load_4d_pair(st + n * spi * (kVKeys * 128), &p.tv, fb, 0, key0 + v * kVKeys,
-                               dim / kChunk, w.b);
+                               dim / E::kCols, w.b);
             }
           }
         };
@@ -278,7 +322,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           const int key0 = w.k_begin + j * kKeys;
           const int valid = min(kKeys, w.k_end - key0);
           const int n_qk = (valid + 15) & ~15;
-          const uint32_t idesc = instr_desc(2, 2 * kRows, n_qk, false, false);
+          const uint32_t idesc = instr_desc(E::kFmt, 2 * kRows, n_qk, false, false);
           for (int c = 0; c < n_qk_chunks && ok; ++c) {
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
             if (c == 0) XATTN_TRACE_POINT(2, j);
@@ -288,7 +332,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = smem_desc(st + kk * 32, 16, 1024, kSw128);
               const uint64_t bd = smem_desc(st + 16384 + kk * 32, 16, 1024, kSw128);
-              mma_tf32_ss_pair(t_s, ad, bd, idesc, (c | kk) != 0);
+              mma_pair<T>(t_s, ad, bd, idesc, (c | kk) != 0);
             }
             mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
             if (++s == kStages) { s = 0; phase ^= 1u; }
@@ -322,19 +366,21 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           const int valid = min(kKeys, w.k_end - key0);
           const int n_v = (valid + kVKeys - 1) / kVKeys;
           const uint32_t xb = smem_u32(xbuf + (gj % kXBufs) * kXBytes);
-          const uint32_t idesc_pv = instr_desc(2, 2 * kRows, nn, false, true);
+          const uint32_t idesc_pv = instr_desc(E::kFmt, 2 * kRows, nn, false, true);
           for (int v = 0; v < n_v; ++v) {
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
             tc_fence_after();
             const uint32_t st = smem_u32(stages + s * kStageBytes);
-            const int ksteps = min(kVKeys / 8, (valid - v * kVKeys + 7) / 8);
+            const int ksteps = min(kVKeys / E::kKStep, (valid - v * kVKeys + E::kKStep - 1) / E::kKStep);
             for (int kk = 0; kk < ksteps; ++kk) {
-              const int key = v * kVKeys + kk * 8;
-              const uint64_t ad = smem_desc(xb + (key >> 5) * 16384 + (key & 31) * 4, 16, 1024, kSw128);
+              const int key = v * kVKeys + kk * E::kKStep;
+              // P: K-major, kCols keys per 128-byte row, 16 KB per key group
+              const uint64_t ad = smem_desc(xb + (key / E::kCols) * 16384 + (key % E::kCols) * sizeof(T),
+                                            16, 1024, kSw128);
               for (int n = 0; n < n_instr; ++n) {
-                const uint64_t bd = smem_desc(st + n * spi * (kVKeys * 128) + kk * 1024,
-                                              kVKeys * 128, 512, kSw128Atom32);
-                mma_tf32_ss_pair(tmem + n * nn, ad, bd, idesc_pv, (j | v | kk) != 0);
+                const uint64_t bd = smem_desc(st + n * spi * (kVKeys * 128) + kk * E::kKStep * 128,
+                                              kVKeys * 128, E::kVSbo, E::kVSwz);
+                mma_pair<T>(tmem + n * nn, ad, bd, idesc_pv, (j | v | kk) != 0);
               }
             }
             mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
@@ -371,6 +417,19 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     bool ok = true;
     int g = 0;   // global index of the item's first tile
     int it = 0;  // items with tiles done
+    // Exchange permissions: the tiles of the cluster's first item with tiles, at most two,
+    // find both of the D-peer's buffers free; every later tile t waits for the peer's
+    // release (phase t - n_impl of x_empty).  (A later item's first tile can be global tile
+    // 1 when the first item has a single tile: it must wait too, since the peer's epilogue
+    // stages the output in these buffers.)
+    int n_impl = 0;
+    for (int i2 = cid; i2 < p.n_items; i2 += n_clusters) {
+      const int nt = item_at(i2).n_tiles;
+      if (nt > 0) {
+        n_impl = min(kXBufs, nt);
+        break;
+      }
+    }
     for (int item = cid; item < p.n_items; item += n_clusters) {
       const Item w = item_at(item);
       const int b = w.b, split = w.split, row0 = w.row0;
@@ -405,9 +464,9 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_remote(lead_s_free);
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
       }
-      // the D-peer's buffer gj % 2 is free for this tile once it signalled so (tiles >= 2)
-      if (ok && gj >= kXBufs)
-        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (gj - kXBufs) & 1, kTimeoutExchange, abort);
+      // the D-peer's buffer gj % 2 is free for this tile once it signalled so (gj >= n_impl)
+      if (ok && gj >= n_impl)
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (gj - n_impl) & 1, kTimeoutExchange, abort);
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
 #pragma unroll
@@ -475,17 +534,38 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       }
       l_run *= alpha;
       float lsum = 0.f;
+      if constexpr (sizeof(T) == 4) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        uint32_t q4[4];
+        for (int i = 0; i < 16; ++i) {
+          uint32_t q4[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const uint32_t tv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
-          q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
-          lsum += __uint_as_float(q4[e]);
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t tv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
+            q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
+            lsum += __uint_as_float(q4[e]);
+          }
+          *reinterpret_cast<uint4*>(xcur + p_offset(ch0 + i, row)) =
+              make_uint4(q4[0], q4[1], q4[2], q4[3]);
         }
-        *reinterpret_cast<uint4*>(xcur + p_offset(ch0 + i, row)) =
-            make_uint4(q4[0], q4[1], q4[2], q4[3]);
+      } else {
+        // fp16 P: this thread's 64 keys are one 128-byte swizzle row of key group grp; the
+        // row sum adds the rounded weights the P.V product uses
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t h4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int k = 8 * c + 2 * e;
+            const uint32_t t0 = k < 32 ? ra[k] : rb[k - 32], t1 = k + 1 < 32 ? ra[k + 1] : rb[k + 1 - 32];
+            const __half2 hv = __floats2half2_rn(ex2_approx(__uint_as_float(t0) - m_run),
+                                                 ex2_approx(__uint_as_float(t1) - m_run));
+            const float2 back = __half22float2(hv);
+            lsum += back.x + back.y;
+            h4[e] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(xcur + grp * 16384 + row * 128 + ((c ^ (row & 7)) << 4)) =
+              make_uint4(h4[0], h4[1], h4[2], h4[3]);
+        }
       }
       l_run += lsum;
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(16, j);
@@ -497,9 +577,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
       if (gj >= 1 && j + 1 < w.n_tiles) {
         // my buffer (gj+1) % 2 held P of tile gj-1; once that P.V completed the D-peer may
-        // send tile gj+1 into it.  Every global tile t >= 2 is released exactly once: here
-        // by the end of tile t-1 of the same item, or after the previous item's epilogue
-        // (which stages the output in these buffers) for an item's first tile.  Consecutive
+        // send tile gj+1 into it.  Every global tile t >= n_impl is released exactly once:
+        // here by the end of tile t-1 of the same item (then t >= 2 >= n_impl), or after the
+        // previous item's epilogue (which stages the output in these buffers) for an item's
+        // first tile.  Consecutive
         // releases from one warp are separated by the all-warp barrier of a tile, so no
         // warp's arrival counts toward another release's phase.
         if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(gj + 1) % kXBufs]),
@@ -543,7 +624,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       // the staging has been read: the D-peer may send the next item's first tile into my
       // buffer (g + n_tiles) % 2, whose last P.V (tile g + n_tiles - 2) is complete
-      if (g + w.n_tiles >= kXBufs && item + n_clusters < p.n_items && lane == 0)
+      if (g + w.n_tiles >= n_impl && item + n_clusters < p.n_items && lane == 0)
         mbar_arrive_remote(peer_x_empty);
     } else if (w.n_tiles == 0 && p.split_mode && live) {
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;

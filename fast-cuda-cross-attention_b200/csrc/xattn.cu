@@ -73,7 +73,10 @@ int prepare_device(int* dev_out) {
     if (cudaFuncSetAttribute(fused::fused_tf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              fused::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
-    if (cudaFuncSetAttribute(pair4::fused_tf32_pair_kernel,
+    if (cudaFuncSetAttribute(pair4::fused_tf32_pair_kernel<float>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             pair4::kSmemBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(pair4::fused_tf32_pair_kernel<__half>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              pair4::kSmemBytes) != cudaSuccess)
       return XATTN_ERR_LAUNCH;
@@ -85,7 +88,7 @@ int prepare_device(int* dev_out) {
       cfg.blockDim = dim3(pair4::kThreads);
       cfg.dynamicSmemBytes = pair4::kSmemBytes;
       int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(pair4::fused_tf32_pair_kernel),
+      if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(pair4::fused_tf32_pair_kernel<float>),
                                          &cfg) == cudaSuccess && n > 0)
         st.pair_slots = n;
       else
@@ -238,41 +241,57 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 
-// Four-CTA pair kernel, normalised output (fused_tf32_pair.cuh).
-int launch_fused_pair(const float* Q, const float* K, const float* V, float* out, int B, int Nl,
-                      int Ni, int D, cudaStream_t stream, float score_scale = -1.f,
+// Four-CTA pair kernel (fused_tf32_pair.cuh) on fp32 (kind::tf32) or fp16 (kind::f16)
+// operands.  split_mode = 0: normalised output `out`; 1: partial triples po / pm / pl over
+// num_splits key chunks of split_chunk keys.
+template <typename T>
+int launch_fused_pair(const T* Q, const T* K, const T* V, float* out, float* po, float* pm,
+                      float* pl, int B, int Nl, int Ni, int D, int num_splits, int split_chunk,
+                      int split_mode, cudaStream_t stream, float score_scale = -1.f,
                       bool exact_inputs = false) {
+  using E = pair4::Elem<T>;
+  constexpr CUtensorMapDataType dt =
+      sizeof(T) == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  constexpr uint64_t es = sizeof(T);
+  const int dh = D / 2;
+  if (!E::supports(dh)) return XATTN_ERR_ARG;
   fused::Params p;
-  if (!make_fp32_maps(p, Q, K, V, B, Nl, Ni, D, fused::kKeys / 2, pair4::kVKeys))
-    return XATTN_ERR_ARG;
   {
-    // V as [B][D/32 slabs][Ni keys][32 columns]: one box holds all the 32-column slabs a CTA
-    // needs for one P.V instruction (dh / n_instr / 2 columns), so a V stage is one or two
-    // copies instead of up to six.
-    const int dh = D / 2;
-    const int spi = dh / (dh <= 256 ? 1 : 2) / 64;
-    const uint64_t dv[4] = {(uint64_t)fused::kChunk, (uint64_t)Ni, (uint64_t)D / fused::kChunk,
-                            (uint64_t)B};
-    const uint64_t sv[3] = {(uint64_t)D * 4, (uint64_t)fused::kChunk * 4, (uint64_t)Ni * D * 4};
-    const uint32_t bv[4] = {fused::kChunk, pair4::kVKeys, (uint32_t)spi, 1};
-    if (!encode_tmap(&p.tv, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, V, dv, sv, bv,
-                     CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    const uint64_t dq[3] = {(uint64_t)D, (uint64_t)Nl, (uint64_t)B};
+    const uint64_t sq[2] = {(uint64_t)D * es, (uint64_t)Nl * D * es};
+    const uint64_t dk[3] = {(uint64_t)D, (uint64_t)Ni, (uint64_t)B};
+    const uint64_t sk[2] = {(uint64_t)D * es, (uint64_t)Ni * D * es};
+    const uint32_t bq[3] = {(uint32_t)E::kCols, fused::kRows, 1};
+    const uint32_t bk[3] = {(uint32_t)E::kCols, fused::kKeys / 2, 1};
+    // V as [B][D/kCols slabs][Ni keys][kCols columns]: one box holds all the slabs a CTA
+    // needs for one P.V instruction (dh / n_instr / 2 columns), so a V stage is one copy
+    // per instruction
+    const int spi = dh / E::n_instr(dh) / (2 * E::kCols);
+    const uint64_t dv[4] = {(uint64_t)E::kCols, (uint64_t)Ni, (uint64_t)D / E::kCols, (uint64_t)B};
+    const uint64_t sv[3] = {(uint64_t)D * es, (uint64_t)E::kCols * es, (uint64_t)Ni * D * es};
+    const uint32_t bv[4] = {(uint32_t)E::kCols, (uint32_t)E::kVKeys, (uint32_t)spi, 1};
+    if (!encode_tmap(&p.tq, dt, 3, Q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&p.tk, dt, 3, K, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&p.tv, dt, 4, V, dv, sv, bv,
+                     sizeof(T) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B))
       return XATTN_ERR_ARG;
   }
-  if (!make_out_map(p, out, nullptr, B, Nl, D, 1, 0)) return XATTN_ERR_ARG;
+  if (!make_out_map(p, out, po, B, Nl, D, num_splits, split_mode)) return XATTN_ERR_ARG;
   p.out = out;
-  p.po = p.pm = p.pl = nullptr;
+  p.po = po;
+  p.pm = pm;
+  p.pl = pl;
   p.batch = B;
   p.n_latent = Nl;
   p.n_input = Ni;
   p.dim = D;
-  p.dh = D / 2;
+  p.dh = dh;
   p.n_row_blocks = (Nl + 2 * fused::kRows - 1) / (2 * fused::kRows);
-  p.num_splits = 1;
-  p.split_chunk = Ni;
-  p.split_mode = 0;
+  p.num_splits = num_splits;
+  p.split_chunk = split_chunk;
+  p.split_mode = split_mode;
   set_scale(p, D, score_scale, exact_inputs);
-  const long long items = static_cast<long long>(B) * p.n_row_blocks;
+  const long long items = static_cast<long long>(B) * p.n_row_blocks * num_splits;
   if (items * 4 > 0x7fffffffLL) return XATTN_ERR_ARG;
   p.n_items = static_cast<int>(items);
   // persistent: one cluster per co-resident slot, each looping over items
@@ -280,9 +299,16 @@ int launch_fused_pair(const float* Q, const float* K, const float* V, float* out
   cudaGetDevice(&dev);
   const int slots = dev >= 0 && dev < 64 ? g_dev[dev].pair_slots : 0;
   const long long clusters = slots > 0 ? std::min<long long>(items, slots) : items;
-  pair4::fused_tf32_pair_kernel<<<static_cast<unsigned>(clusters * 4), pair4::kThreads,
-                                  pair4::kSmemBytes, stream>>>(p);
+  pair4::fused_tf32_pair_kernel<T><<<static_cast<unsigned>(clusters * 4), pair4::kThreads,
+                                     pair4::kSmemBytes, stream>>>(p);
   return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
+int launch_fused_pair(const float* Q, const float* K, const float* V, float* out, int B, int Nl,
+                      int Ni, int D, cudaStream_t stream, float score_scale = -1.f,
+                      bool exact_inputs = false) {
+  return launch_fused_pair<float>(Q, K, V, out, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni, 0,
+                                  stream, score_scale, exact_inputs);
 }
 
 // The pair kernel pays off once 256-row blocks fill the four-CTA cluster slots
@@ -558,6 +584,41 @@ int run_half(const __half* Q, const __half* K, const __half* V, float* O, float*
                                     kLog2e, stream);
     if (rc != XATTN_OK) return rc;
     return launch_combine(po, pm, pl, O, static_cast<long long>(B) * Nl, D, S, stream);
+  }
+  // Native fp16: the pair kernel on kind::f16 operands (D halves that split into whole
+  // 64-column slabs per P.V instruction: D = 256, 512, 768), Q pre-scaled by the caller.
+  // Key splits fill the cluster slots when there are fewer 256-row blocks than slots.
+  if (pair4::Elem<__half>::supports(D / 2) && g_opt_kernel.load() != 1) {
+    const long long rows_all = static_cast<long long>(B) * Nl;
+    if (S > 0) {  // upstream split-K entry: caller scratch, chunk rounded up to 16 keys
+      rc = launch_fused_pair<__half>(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, S, chunk16, 1,
+                                     stream, 1.f, true);
+      if (rc != XATTN_OK) return rc;
+      return launch_combine(po, pm, pl, O, rows_all, D, S, stream);
+    }
+    const long long items = static_cast<long long>(B) * ((Nl + 255) / 256);
+    const int n_tiles = (Ni + fused::kKeys - 1) / fused::kKeys;
+    const int slots = g_dev[dev].pair_slots > 0 ? g_dev[dev].pair_slots : std::max(1, sm_count(dev) / 4);
+    int splits = g_opt_splits.load();
+    if (splits <= 0)
+      splits = items < slots ? static_cast<int>(std::min<long long>(n_tiles, slots / items)) : 1;
+    splits = std::max(1, std::min(splits, n_tiles));
+    const int chunk = (n_tiles + splits - 1) / splits * fused::kKeys;
+    splits = (Ni + chunk - 1) / chunk;
+    if (splits == 1)
+      return launch_fused_pair<__half>(Q, K, V, O, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni,
+                                       0, stream, 1.f, true);
+    const size_t po_n = static_cast<size_t>(rows_all) * splits * D, ml_n = static_cast<size_t>(rows_all) * splits;
+    auto r64 = [](size_t n) { return (n + 63) / 64 * 64; };
+    float* ws = static_cast<float*>(workspace(dev, stream, (r64(po_n) + 2 * r64(ml_n)) * sizeof(float)));
+    if (ws == nullptr) return XATTN_ERR_NOMEM;
+    float* wpo = ws;
+    float* wpm = wpo + r64(po_n);
+    float* wpl = wpm + r64(ml_n);
+    rc = launch_fused_pair<__half>(Q, K, V, nullptr, wpo, wpm, wpl, B, Nl, Ni, D, splits, chunk, 1,
+                                   stream, 1.f, true);
+    if (rc != XATTN_OK) return rc;
+    return launch_combine(wpo, wpm, wpl, O, rows_all, D, splits, stream);
   }
   // plan first, so one workspace request covers the widened inputs and any split partials
   const bool pair = S == 0 && g_opt_splits.load() <= 0 && use_pair_kernel(dev, B, Nl, D);

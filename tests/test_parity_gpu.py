@@ -148,6 +148,9 @@ def test_fp32_shapes_with_guards(X, torch_cuda, shape):
 PAIR_SHAPES = [
     (2, 256, 784, 768), (1, 200, 300, 768), (3, 129, 129, 512), (2, 300, 1000, 256),
     (1, 64, 100, 128), (4, 512, 784, 384), (1, 1, 1, 768),
+    # more 256-row items than co-resident clusters (33 on a B200): the persistent clusters
+    # loop over items with one, two and several key tiles each
+    (40, 256, 100, 768), (36, 512, 200, 768), (70, 256, 300, 256), (40, 256, 784, 768),
 ]
 
 
@@ -380,8 +383,9 @@ FP16_SHAPES = [(2, 64, 784, 768), (16, 1024, 784, 768), (3, 130, 300, 512), (1, 
 def test_fp16_entries_tensor_core(X, torch_cuda, shape, splits):
     """launch_wmma_kernel (splits = 0) and launch_wmma_splitk_kernel against float64 on the
     exact fp16 values, Q pre-scaled by 1/sqrt(D) as upstream callers do
-    (cuda_wrappers.py:635-640).  fp16 values are exact in TF32, so the tensor-core path
-    meets the TF32 tolerance with room to spare."""
+    (cuda_wrappers.py:635-640).  D = 256, 512, 768 run the kind::f16 pair kernel (fp16
+    products are exact in the fp32 accumulator, P rounded to fp16 like TF32's 10-bit
+    mantissa); D = 64 widens to fp32 for the TF32 kernels.  Both meet the TF32 tolerance."""
     import ctypes
 
     torch = torch_cuda
@@ -410,6 +414,39 @@ def test_fp16_entries_tensor_core(X, torch_cuda, shape, splits):
     assert intact()
     exact = torch.softmax(q.double() @ k.double().transpose(1, 2), -1) @ v.double()
     assert_close(torch, out.double(), exact, TF32_TOL, f"fp16 {shape} S={splits}")
+    assert X.device_status() == 0
+
+
+@pytest.mark.parametrize("shape", [(16, 1024, 784, 768), (2, 200, 1000, 256), (1, 64, 784, 512)])
+def test_fp16_native_and_widened_paths_agree(X, torch_cuda, shape):
+    """The kind::f16 pair kernel against the fp16 -> fp32 widening path on the TF32 kernels
+    (forced with option 5 = 1), and both against float64."""
+    import ctypes
+
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    gen = torch.Generator(device="cuda").manual_seed(37)
+    q = (torch.randn(b, nl, d, device="cuda", generator=gen) / math.sqrt(d)).half()
+    k, v = (torch.randn(b, ni, d, device="cuda", generator=gen).half() for _ in range(2))
+    lib = X.lib()
+    P, I = ctypes.c_void_p, ctypes.c_int
+    lib.launch_wmma_kernel.argtypes = [P] * 4 + [I] * 4 + [P]
+    outs = []
+    for sel in (0, 1):
+        prev = X.set_option(X.OPT_KERNEL, sel)
+        try:
+            out = torch.empty(b, nl, d, device="cuda")
+            lib.launch_wmma_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni, d, None)
+            torch.cuda.synchronize()
+            assert lib.xattn_last_error() == 0
+        finally:
+            X.set_option(X.OPT_KERNEL, prev)
+        outs.append(out)
+    exact = torch.softmax(q.double() @ k.double().transpose(1, 2), -1) @ v.double()
+    assert_close(torch, outs[0].double(), exact, TF32_TOL, f"fp16 native {shape}")
+    assert_close(torch, outs[1].double(), exact, TF32_TOL, f"fp16 widened {shape}")
+    scale = exact.abs().max().item()
+    assert (outs[0] - outs[1]).abs().max().item() <= 2 * TF32_TOL * scale
     assert X.device_status() == 0
 
 
