@@ -321,6 +321,21 @@ bool use_pair_kernel(int dev, int B, int Nl, int D) {
   return items >= sm_count(dev) * 2 / 9;
 }
 
+// Key-split plan of the pair kernel: tile-aligned splits so that batch x 256-row blocks x
+// splits fills the co-resident cluster slots (one split when the blocks already do).
+void plan_pair_splits(int dev, int B, int Nl, int Ni, int* splits_out, int* chunk_out) {
+  const long long items = static_cast<long long>(B) * ((Nl + 255) / 256);
+  const int n_tiles = (Ni + fused::kKeys - 1) / fused::kKeys;
+  const int slots = g_dev[dev].pair_slots > 0 ? g_dev[dev].pair_slots : std::max(1, sm_count(dev) / 4);
+  int splits = g_opt_splits.load();
+  if (splits <= 0)
+    splits = items < slots ? static_cast<int>(std::min<long long>(n_tiles, slots / items)) : 1;
+  splits = std::max(1, std::min(splits, std::max(1, n_tiles)));
+  const int chunk = (n_tiles + splits - 1) / splits * fused::kKeys;
+  *splits_out = splits == 1 ? 1 : (Ni + chunk - 1) / chunk;
+  *chunk_out = *splits_out == 1 ? Ni : chunk;
+}
+
 // ------------------------------------------------------------------ generic path
 template <typename Tin, typename Tout>
 int launch_simt(const Tin* Q, const Tin* K, const Tin* V, Tout* out, float* po, float* pm,
@@ -407,6 +422,47 @@ void plan_splits(int dev, int B, int Nl, int Ni, int path, int* splits_out, int*
   if (splits == 1) chunk = Ni;
   *splits_out = splits;
   *chunk_out = chunk;
+}
+
+// Tensor-core fp32 attention with automatic key splits.  partial = false: normalised output
+// `out`; true: the (m, l, O) triple of all keys into po / pm / pl.  The four-CTA pair kernel
+// takes every D it supports (its row pairs share each K/V tile, 384 KB of operands per CTA
+// and tile against the two-CTA kernel's 576 KB); key splits fill its cluster slots when the
+// 256-row blocks cannot (C4: 2206 -> 1660 us).  option 5 = 1 forces the two-CTA kernel.
+int run_fused_auto(int dev, const float* Q, const float* K, const float* V, float* out, float* po,
+                   float* pm, float* pl, int B, int Nl, int Ni, int D, bool partial,
+                   cudaStream_t stream) {
+  const bool pair = g_opt_kernel.load() != 1 && pair4::supports_dh(D / 2) && Ni > 0;
+  int splits = 1, chunk = std::max(1, Ni);
+  if (Ni > 0) {
+    if (pair)
+      plan_pair_splits(dev, B, Nl, Ni, &splits, &chunk);
+    else
+      plan_splits(dev, B, Nl, Ni, g_opt_path.load(), &splits, &chunk);
+  }
+  if (splits == 1) {
+    if (pair)
+      return partial ? launch_fused_pair<float>(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, 1, Ni, 1, stream)
+                     : launch_fused_pair(Q, K, V, out, B, Nl, Ni, D, stream);
+    return partial ? launch_fused(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, 1, chunk, 1, stream)
+                   : launch_fused(Q, K, V, out, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni, 0, stream);
+  }
+  // Tile-aligned key split through the library workspace, then the log-sum-exp merge.
+  const size_t rows = static_cast<size_t>(B) * Nl;
+  const size_t po_n = rows * splits * D, ml_n = rows * splits;
+  auto r64 = [](size_t n) { return (n + 63) / 64 * 64; };
+  float* ws = static_cast<float*>(workspace(dev, stream, (r64(po_n) + 2 * r64(ml_n)) * sizeof(float)));
+  if (ws == nullptr) return XATTN_ERR_NOMEM;
+  float* wpo = ws;
+  float* wpm = wpo + r64(po_n);
+  float* wpl = wpm + r64(ml_n);
+  const int rc = pair ? launch_fused_pair<float>(Q, K, V, nullptr, wpo, wpm, wpl, B, Nl, Ni, D, splits,
+                                                 chunk, 1, stream)
+                      : launch_fused(Q, K, V, nullptr, wpo, wpm, wpl, B, Nl, Ni, D, splits, chunk, 1,
+                                     stream);
+  if (rc != XATTN_OK) return rc;
+  return partial ? launch_combine(wpo, wpm, wpl, po, static_cast<long long>(rows), D, splits, stream, pm, pl)
+                 : launch_combine(wpo, wpm, wpl, out, static_cast<long long>(rows), D, splits, stream);
 }
 
 // The fp32 entry: all four upstream fp32 names and xattn_fp32 land here.
@@ -517,25 +573,8 @@ int run_fp32(const float* Q, const float* K, const float* V, float* O, int B, in
     return set_error(launch_simt<float, float>(Q, K, V, O, nullptr, nullptr, nullptr, B, 1, Nl, Ni,
                                                D, 1, Ni, 0, scale_log2, stream));
   }
-  if (g_opt_splits.load() <= 0 && use_pair_kernel(dev, B, Nl, D))
-    return set_error(launch_fused_pair(Q, K, V, O, B, Nl, Ni, D, stream));
-  int splits = 1, chunk = Ni;
-  plan_splits(dev, B, Nl, Ni, path, &splits, &chunk);
-  if (splits == 1)
-    return set_error(launch_fused(Q, K, V, O, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni, 0,
+  return set_error(run_fused_auto(dev, Q, K, V, O, nullptr, nullptr, nullptr, B, Nl, Ni, D, false,
                                   stream));
-  // Tile-aligned key split through the library workspace, then the log-sum-exp merge.
-  const size_t rows = static_cast<size_t>(B) * Nl;
-  const size_t po_elems = rows * splits * D;
-  const size_t ml_elems = rows * splits;
-  float* ws = static_cast<float*>(workspace(dev, stream, (po_elems + 2 * ml_elems + 64) * sizeof(float)));
-  if (ws == nullptr) return set_error(XATTN_ERR_NOMEM);
-  float* po = ws;
-  float* pm = po + po_elems;
-  float* pl = pm + ml_elems;
-  rc = launch_fused(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, splits, chunk, 1, stream);
-  if (rc != XATTN_OK) return set_error(rc);
-  return set_error(launch_combine(po, pm, pl, O, static_cast<long long>(rows), D, splits, stream));
 }
 
 int run_splitk(const float* Q, const float* K, const float* V, float* O, float* po, float* pm,
@@ -553,6 +592,8 @@ int run_splitk(const float* Q, const float* K, const float* V, float* O, float* 
   if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, O, D) || !aligned16(po))
     rc = launch_simt<float, float>(Q, K, V, nullptr, po, pm, pl, B, 1, Nl, Ni, D, S, chunk, 1,
                                    scale_log2, stream);
+  else if (g_opt_kernel.load() != 1 && pair4::supports_dh(D / 2))
+    rc = launch_fused_pair<float>(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, S, chunk, 1, stream);
   else
     rc = launch_fused(Q, K, V, nullptr, po, pm, pl, B, Nl, Ni, D, S, chunk, 1, stream);
   if (rc != XATTN_OK) return set_error(rc);
@@ -596,15 +637,8 @@ int run_half(const __half* Q, const __half* K, const __half* V, float* O, float*
       if (rc != XATTN_OK) return rc;
       return launch_combine(po, pm, pl, O, rows_all, D, S, stream);
     }
-    const long long items = static_cast<long long>(B) * ((Nl + 255) / 256);
-    const int n_tiles = (Ni + fused::kKeys - 1) / fused::kKeys;
-    const int slots = g_dev[dev].pair_slots > 0 ? g_dev[dev].pair_slots : std::max(1, sm_count(dev) / 4);
-    int splits = g_opt_splits.load();
-    if (splits <= 0)
-      splits = items < slots ? static_cast<int>(std::min<long long>(n_tiles, slots / items)) : 1;
-    splits = std::max(1, std::min(splits, n_tiles));
-    const int chunk = (n_tiles + splits - 1) / splits * fused::kKeys;
-    splits = (Ni + chunk - 1) / chunk;
+    int splits = 1, chunk = Ni;
+    plan_pair_splits(dev, B, Nl, Ni, &splits, &chunk);
     if (splits == 1)
       return launch_fused_pair<__half>(Q, K, V, O, nullptr, nullptr, nullptr, B, Nl, Ni, D, 1, Ni,
                                        0, stream, 1.f, true);
@@ -758,23 +792,8 @@ extern "C" int xattn_fp32_partial(const float* Q, const float* K, const float* V
                                                scale_log2, stream));
   // Key splits when the row blocks alone cannot fill the GPU, as for the plain entry; the
   // splits' partials are then merged into the one (m, l, O) triple asked for.
-  int splits = 1, chunk = std::max(1, N_input);
-  if (N_input > 0) plan_splits(dev, batch_size, N_latent, N_input, path, &splits, &chunk);
-  if (splits == 1)
-    return set_error(launch_fused(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim,
-                                  1, std::max(1, N_input), 1, stream));
-  const size_t rows = static_cast<size_t>(batch_size) * N_latent;
-  const size_t po_elems = rows * splits * dim, ml_elems = rows * splits;
-  float* ws = static_cast<float*>(workspace(dev, stream, (po_elems + 2 * ml_elems + 64) * sizeof(float)));
-  if (ws == nullptr) return set_error(XATTN_ERR_NOMEM);
-  float* wpo = ws;
-  float* wpm = wpo + po_elems;
-  float* wpl = wpm + ml_elems;
-  rc = launch_fused(Q, K, V, nullptr, wpo, wpm, wpl, batch_size, N_latent, N_input, dim, splits,
-                    chunk, 1, stream);
-  if (rc != XATTN_OK) return set_error(rc);
-  return set_error(launch_combine(wpo, wpm, wpl, po, static_cast<long long>(rows), dim, splits,
-                                  stream, pm, pl));
+  return set_error(run_fused_auto(dev, Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input,
+                                  dim, true, stream));
 }
 
 extern "C" int xattn_combine(const float* po, const float* pm, const float* pl, float* output,
@@ -889,7 +908,11 @@ extern "C" int xattn_plan_fp32(int batch_size, int N_latent, int N_input, int di
     int dev = 0;
     if (prepare_device(&dev) != XATTN_OK) return -1;
     const bool tc = dim >= 64 && dim <= 2 * fused::kMaxDh && dim % 64 == 0 && g_opt_path.load() != 2;
-    if (tc) plan_splits(dev, batch_size, N_latent, N_input, g_opt_path.load(), &splits, &chunk);
+    const bool pair = tc && g_opt_kernel.load() != 1 && pair4::supports_dh(dim / 2);  // as run_fused_auto
+    if (pair)
+      plan_pair_splits(dev, batch_size, N_latent, N_input, &splits, &chunk);
+    else if (tc)
+      plan_splits(dev, batch_size, N_latent, N_input, g_opt_path.load(), &splits, &chunk);
     launches = splits > 1 ? 2 : 1;
   } else if (batch_size > 0 && N_latent > 0 && N_input == 0) {
     launches = 1;  // the zero fill
