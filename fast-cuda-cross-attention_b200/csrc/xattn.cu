@@ -1,11 +1,14 @@
 // kernels.so: the C ABI declared in include/xattn.h and the host-side dispatch behind it.
 //
 // Path selection for an fp32 call (Q, K, V, O fp32, row-major, contiguous):
-//   * tensor-core path (fused_tf32.cuh) when D is a multiple of 64 in [64, 768] and the
-//     four pointers are 16-byte aligned (TMA requirement); a key split with a library
-//     workspace is added automatically when batch * ceil(N_latent/128) row blocks cannot
-//     fill the GPU's SMs;
+//   * tensor-core path when D is a multiple of 64 in [64, 768] and the four pointers are
+//     16-byte aligned (TMA requirement): the persistent four-CTA pair kernel
+//     (fused_tf32_pair.cuh) for D in {128, 256, 384, 512, 768}, the two-CTA kernel
+//     (fused_tf32.cuh) for the other D; a key split through a library workspace and the
+//     LSE combine is added automatically when the row blocks cannot fill the cluster slots;
 //   * generic CUDA-core path (simt.cuh) otherwise.
+// fp16 calls run the pair kernel on kind::f16 operands for D in {256, 512, 768}, else widen
+// to fp32 (exact) for the paths above; bf16 multi-head calls run mha_bf16.cuh.
 // There is no host fallback: every path is a GPU kernel.
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -403,7 +406,8 @@ int zero_output(float* O, int B, int Nl, int D, cudaStream_t stream) {
 }
 
 // Key-split plan of the automatic fp32 path: one pass when batch * row blocks fill the
-// two-CTA cluster slots (SMs / 2), otherwise enough tile-aligned splits to fill them.
+// two-CTA cluster slots (SMs / 2), otherwise enough tile-aligned splits to fill them
+// (used for the two-CTA kernel; the pair kernel plans with plan_pair_splits).
 void plan_splits(int dev, int B, int Nl, int Ni, int path, int* splits_out, int* chunk_out) {
   const int n_rb = (Nl + fused::kRows - 1) / fused::kRows;
   const long long items = static_cast<long long>(B) * n_rb;
@@ -428,7 +432,7 @@ void plan_splits(int dev, int B, int Nl, int Ni, int path, int* splits_out, int*
 // `out`; true: the (m, l, O) triple of all keys into po / pm / pl.  The four-CTA pair kernel
 // takes every D it supports (its row pairs share each K/V tile, 384 KB of operands per CTA
 // and tile against the two-CTA kernel's 576 KB); key splits fill its cluster slots when the
-// 256-row blocks cannot (C4: 2206 -> 1660 us).  option 5 = 1 forces the two-CTA kernel.
+// 256-row blocks cannot (C4: 2206 -> 1614 us).  option 5 = 1 forces the two-CTA kernel.
 int run_fused_auto(int dev, const float* Q, const float* K, const float* V, float* out, float* po,
                    float* pm, float* pl, int B, int Nl, int Ni, int D, bool partial,
                    cudaStream_t stream) {
@@ -601,12 +605,13 @@ int run_splitk(const float* Q, const float* K, const float* V, float* O, float* 
 }
 
 // fp16 entries (upstream kernel_wmma.cu / kernel_wmma_splitk.cu; Q pre-scaled by 1/sqrt(D)
-// on the host, cuda_wrappers.py:635-640).  Every fp16 value is exactly representable in
-// TF32, so the inputs are widened to fp32 in the library workspace and the tcgen05 TF32
-// kernels compute exactly the products an fp16 MMA would (fp32 accumulation), with score
-// scale 1 and no truncation compensation.  S = 0: the plain entry (automatic kernel and key
-// split); S > 0: the split entry, partials into the caller's po/pm/pl with the upstream
-// chunk of max(16, round_up(ceil(Ni/S), 16)) keys (kernel_wmma_splitk.cu:52).  Shapes the
+// on the host, cuda_wrappers.py:635-640), score scale 1.  D in {256, 512, 768}: the pair
+// kernel on kind::f16 operands (fp16 products exact in the fp32 accumulator).  Other
+// tensor-core D: every fp16 value is exactly representable in TF32, so the inputs are
+// widened to fp32 in the library workspace for the TF32 kernels (no truncation
+// compensation).  S = 0: the plain entry (automatic kernel and key split); S > 0: the split
+// entry, partials into the caller's po/pm/pl with the upstream chunk of
+// max(16, round_up(ceil(Ni/S), 16)) keys (kernel_wmma_splitk.cu:52).  Shapes the
 // tensor-core kernels do not take run the generic kernel on the fp16 data directly.
 int run_half(const __half* Q, const __half* K, const __half* V, float* O, float* po, float* pm,
              float* pl, int B, int Nl, int Ni, int D, int S, cudaStream_t stream) {

@@ -56,7 +56,9 @@ void launch_optimized_kernel(const float* Q, const float* K, const float* V, flo
 
 /* Replaces launch_wmma_kernel (kernel_wmma.cu:139-154; cuda_wrappers.py:136-146).
  * fp16 Q (already multiplied by 1/sqrt(dim) by the caller, cuda_wrappers.py:635-640),
- * fp16 K, V; fp32 output.  Any N_latent / N_input (upstream needs multiples of 16).     */
+ * fp16 K, V; fp32 output.  Any N_latent / N_input (upstream needs multiples of 16).
+ * dim in {256, 512, 768}: tcgen05 kind::f16 tensor cores; other multiples of 64: the
+ * fp16 values widened (exactly) to fp32 for the TF32 kernels.                           */
 void launch_wmma_kernel(const __half* Q, const __half* K, const __half* V, float* output,
                         int batch_size, int N_latent, int N_input, int dim,
                         cudaStream_t stream);
