@@ -1,17 +1,24 @@
-// Fused fp32-API cross attention on 4-CTA clusters: a cta_group::2 row pair per D half.
+// Fused cross attention on 4-CTA clusters: a cta_group::2 row pair per D half, on fp32
+// operands (kind::tf32, the fp32 API) or fp16 operands (kind::f16, the upstream WMMA entries).
 //
-// Same computation and epilogue as fused_tf32.cuh (read that file first); this variant
-// changes how one SM's share of the work is fed.  A cluster of four CTAs owns 256 query rows
-// of one batch:  rank = 2h + r, where h is the half of D the CTA owns (as in the two-CTA
-// kernel) and r the 128-row half.  The two CTAs with the same h form a cta_group::2 pair:
-// the pair leader (r = 0) issues every MMA for both, with M = 256 rows; the K operand of
-// Q.K^T and the V operand of P.V are split between the pair's shared memories (each CTA
-// loads half the keys of K and half the columns of V), so every K/V byte is loaded once per
-// 256 queries instead of once per 128.  Per key tile and CTA that is 384 KB of operands
-// (Q 192 + K 96 + V 96) instead of 576 KB, and half the shared-memory reads of K and V.
-// Scores are still exchanged between the two D halves (ranks r and r + 2) through
-// distributed shared memory; P stays per CTA (each CTA supplies its own 128 rows of P as
-// the A operand of the pair MMA).
+// Same computation as fused_tf32.cuh (read that file first); this variant changes how one
+// SM's share of the work is fed.  A cluster of four CTAs owns 256 query rows of one batch
+// (and a key range, in split mode):  rank = 2h + r, where h is the half of D the CTA owns
+// (as in the two-CTA kernel) and r the 128-row half.  The two CTAs with the same h form a
+// cta_group::2 pair: the pair leader (r = 0) issues every MMA for both, with M = 256 rows;
+// the K operand of Q.K^T and the V operand of P.V are split between the pair's shared
+// memories (each CTA loads half the keys of K and half the columns of V), so every K/V byte
+// is loaded once per 256 queries instead of once per 128.  Per fp32 key tile and CTA that
+// is 384 KB of operands (Q 192 + K 96 + V 96) instead of 576 KB (fp16: half).  Scores are
+// still exchanged between the two D halves (ranks r and r + 2) through distributed shared
+// memory (fp32 partial scores in both variants); P stays per CTA (each CTA supplies its own
+// 128 rows of P as the A operand of the pair MMA).
+//
+// Persistent: one cluster per co-resident slot loops over the items (batch, 256-row block,
+// key split); the ring, the MMA issuer's ring position and every per-tile barrier phase
+// continue across items on a global tile index, so the next item's operands stream while
+// the current item finishes.  The epilogue stages O (32 x 32 boxes) in the exchange buffers
+// and writes it with TMA stores.
 //
 // Pair protocol.  TMA loads of both CTAs complete on the leader's full barrier; the
 // leader's commits are multicast to both CTAs (empty, s_full, pv_done, o_done); the
@@ -19,11 +26,11 @@
 // leader's s_free / p_full barriers.  No TMA multicast is used.
 //
 // Operand ring.  Three producer warps share one ring of 24 KB stages in the order QK(0),
-// then per tile QK(j+1), V(j): a Q/K stage is a 32-column chunk of the CTA's 128 Q rows and
-// of its half of the K tile, a V stage one 4-D box of 32 keys x the CTA's 32-column slabs.
+// then per tile QK(j+1), V(j): a Q/K stage is a 128-byte-wide chunk of the CTA's 128 Q rows
+// and of its half of the K tile, a V stage one 4-D box of keys x the CTA's V slabs.
 // Producer 0 also prefetches into L2 the V of the tile being loaded and each producer the
 // next tile's K chunk it will load, so fewer stage round trips wait on DRAM.  The stream of
-// stages through this ring, not the softmax, sets the pace of the kernel: its depth is
+// stages through this ring, not the softmax, sets the pace of the fp32 kernel: its depth is
 // bounded by the 128 KB of exchange / P buffers beside it.
 #pragma once
 
