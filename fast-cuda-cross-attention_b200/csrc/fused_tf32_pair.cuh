@@ -21,17 +21,25 @@
 // and writes it with TMA stores.
 //
 // Pair protocol.  TMA loads of both CTAs complete on the leader's full barrier; the
-// leader's commits are multicast to both CTAs (empty, s_full, pv_done, o_done); the
+// leader's commits are multicast to both CTAs (empty, s_full, pv_done, o_done) or to the
+// D-peer pair (x_empty); the
 // softmax warps of both CTAs release S and publish P by one arrival per warp on the
 // leader's s_free / p_full barriers.  No TMA multicast is used.
 //
-// Operand ring.  Three producer warps share one ring of 24 KB stages in the order QK(0),
-// then per tile QK(j+1), V(j): a Q/K stage is a 128-byte-wide chunk of the CTA's 128 Q rows
-// and of its half of the K tile, a V stage one 4-D box of keys x the CTA's V slabs.
+// Operand ring.  Three producer warps share one ring of five 24 KB stages in the order
+// QK(0), then per tile QK(j+1), V(j): a Q/K stage is a 128-byte-wide chunk of the CTA's 128
+// Q rows and of its half of the K tile, a V stage one 4-D box of keys x the CTA's V slabs.
 // Producer 0 also prefetches into L2 the V of the tile being loaded and each producer the
 // next tile's K chunk it will load, so fewer stage round trips wait on DRAM.  The stream of
 // stages through this ring, not the softmax, sets the pace of the fp32 kernel: its depth is
-// bounded by the 128 KB of exchange / P buffers beside it.
+// bounded by the exchange / P slots beside it.
+//
+// Exchange slots.  The partial scores travel in pieces of half a key tile (one softmax
+// group's 64 keys): piece use u = 2 g + group of global tile g lands in slot u % 3 of the
+// D-peer, where the peer's softmax then writes P over it.  The pair leader hands a slot back
+// to the D-peer pair with a commit multicast to both of its CTAs once the P.V instructions
+// that read the piece complete (an arrival on their x_empty barrier, no data), so the next
+// tile's second piece waits only for the first half of this tile's P.V.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -99,11 +107,15 @@ __device__ __forceinline__ void mma_pair(uint32_t d, uint64_t a, uint64_t b, uin
     mma_f16_ss_pair(d, a, b, idesc, acc);
 }
 constexpr int kStageBytes = 24576;   // Q chunk 16 KB + K half 8 KB, or a V chunk
-// Exchange / P buffers: 2 (the next tile's exchange overlaps this tile's P.V; 4 stages), or
-// 1 (a 6-stage ring, 144 KB of operands in flight, but the exchange then waits for P.V:
-// measured 10 % slower at the headline shape).
-constexpr int kXBufs = 2;
-constexpr int kStages = kXBufs == 1 ? 6 : 4;
+// Exchange / P pieces: half a key tile each (one softmax group's 64 keys x 128 rows, fp32,
+// 32 KB) in a ring of three slots.  Piece use u = 2 g + group of global tile g goes to slot
+// u % 3; the D-peer may send use u once use u - 3 of the slot was consumed by P.V.  Three
+// half-tile slots keep the next tile's exchange overlapping this tile's P.V (its second
+// piece waits only for the first half of P.V) in 96 KB instead of two whole-tile buffers'
+// 128 KB, which leaves room for a fifth ring stage.
+constexpr int kPieceBytes = kXBytes / kGroups;
+constexpr int kXSlots = 3;
+constexpr int kStages = 5;
 // Warps: 0 producer, 1 MMA issuer, 2..9 softmax, 10.. further producers.  Registers are
 // allocated per group of four warps, so twelve warps cost the softmax warps nothing.
 constexpr int kFirstExtraProducer = 2 + kSoftmaxThreads / 32;
@@ -113,14 +125,15 @@ constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (kProducers - 1);
 // alias an older phase because the producer's previous stage, i + kStages - kProducers,
 // already required stage i - kProducers <= i - kStages to be consumed.
 static_assert(kProducers <= kStages, "parity-only empty waits need kProducers <= kStages");
-static_assert(kXBufs == 2, "the exchange permissions below assume double-buffered exchange");
-constexpr int kSmemBytes = kStages * kStageBytes + kXBufs * kXBytes + 1024;
-constexpr int kStaticSmemBytes = 1536;
+constexpr int kXRegion = kXSlots * kPieceBytes;
+constexpr int kSmemBytes = kStages * kStageBytes + kXRegion + 1024;
+constexpr int kStaticSmemBytes = 2048;
 static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
-static_assert(kSoftmaxThreads / 32 * (fused::kMaxDh / 32 / kGroups) * 4096 <=
-                  kStages * kStageBytes + kXBufs * kXBytes,
-              "output staging exceeds the operand buffers");
+// Output staging: the exchange slots, split evenly between the softmax warps in 4 KB boxes.
+constexpr int kStagePerWarp = kXRegion / (kSoftmaxThreads / 32);
+static_assert(kStagePerWarp % 4096 == 0 && kStagePerWarp >= 4096, "output staging boxes");
 constexpr int kSoftmaxWarpsPerPair = 2 * kSoftmaxThreads / 32;
+constexpr int kPieceWarpsPerPair = kSoftmaxWarpsPerPair / kGroups;  // writers of one P piece
 
 // D halves this kernel takes: one pair instruction covers N = dh (dh <= 256) or two of
 // N = dh / 2 (dh = 384); each CTA holds N / 2 columns of V per instruction, whole 32-wide
@@ -132,15 +145,16 @@ struct __align__(8) Barriers {
   uint64_t empty[kStages];  // both: the pair MMA consumed a stage (multicast commit)
   uint64_t s_full;          // both: S tile ready (multicast)
   uint64_t s_free;          // leader: both CTAs copied S out of TMEM
-  uint64_t p_full[kXBufs];  // leader: both CTAs wrote P of tile g (barrier g % 2).  One per
-                            // buffer: the pair CTAs are not synchronised between releasing S
-                            // and publishing P, so one CTA may publish tile g+1 before the
-                            // other publishes tile g (never g+2: Q.K^T(g+2) follows P.V(g))
-  uint64_t pv_done[kXBufs]; // both: P.V on buffer b complete (multicast)
-  uint64_t o_done;          // both: last P.V complete (multicast)
-  uint64_t x_full[kXBufs];  // D-peer -> me: partial scores in my buffer b
-  uint64_t x_empty;         // D-peer -> me: its buffer for my next send may be refilled
-  uint64_t drain;           // leader: its MMAs completed
+  uint64_t p_full[kXSlots];  // leader: both CTAs wrote the P piece in slot b (one barrier per
+                             // slot: the pair CTAs are not synchronised between releasing S
+                             // and publishing P, so one may publish a later piece first)
+  uint64_t pv_done[2];       // both: P.V of tile g complete (barrier g % 2, multicast)
+  uint64_t o_done;           // both: last P.V complete (multicast)
+  uint64_t x_full[kXSlots];  // D-peer -> me: a partial-score piece landed in my slot b
+  uint64_t x_empty[kXSlots]; // the D-peer's slot b may be refilled: one arrival per release,
+                             // by the D-peer pair leader's commit after P.V read the piece, or
+                             // by the D-peer after an epilogue that staged O in its slots
+  uint64_t drain;            // leader: its MMAs completed
 };
 
 template <typename T>
@@ -205,13 +219,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     }
     mbar_init(smem_u32(&bars.s_full), 1);
     mbar_init(smem_u32(&bars.s_free), kSoftmaxWarpsPerPair);
-    for (int i = 0; i < kXBufs; ++i) mbar_init(smem_u32(&bars.p_full[i]), kSoftmaxWarpsPerPair);
-    for (int i = 0; i < kXBufs; ++i) {
-      mbar_init(smem_u32(&bars.pv_done[i]), 1);
+    for (int i = 0; i < kXSlots; ++i) {
+      mbar_init(smem_u32(&bars.p_full[i]), kPieceWarpsPerPair);
       mbar_init(smem_u32(&bars.x_full[i]), 1);
+      mbar_init(smem_u32(&bars.x_empty[i]), 1);
     }
+    for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars.pv_done[i]), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
-    mbar_init(smem_u32(&bars.x_empty), kSoftmaxThreads / 32);
     mbar_init(smem_u32(&bars.drain), 1);
     fence_mbar_init();
   }
@@ -322,6 +336,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       bool ok = true;
       int g = 0;  // global index of the item's first tile
       const uint32_t t_s = tmem + kSCol;
+      const uint16_t peer_mask = static_cast<uint16_t>(3u << (leader ^ 2u));  // the D-peer pair
       for (int item = cid; item < p.n_items && ok; item += n_clusters) {
         const Item w = item_at(item);
         if (w.n_tiles == 0) continue;
@@ -356,6 +371,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         mma_qk(0);
+        const int u_end = 2 * (g + w.n_tiles);  // first piece use of the cluster's next item
         for (int j = 0; j < w.n_tiles && ok; ++j) {
           const int gj = g + j;
           if (j + 1 < w.n_tiles) {
@@ -364,23 +380,40 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             mma_qk(j + 1);
             if (!ok) break;
           }
-          if (!(ok = mbar_wait<true>(smem_u32(&bars.p_full[gj % kXBufs]), (gj / kXBufs) & 1,
-                                     kTimeoutSoftmax, abort)))
-            break;
-          XATTN_TRACE_POINT(4, j);
-          tc_fence_after();
           const int key0 = w.k_begin + j * kKeys;
           const int valid = min(kKeys, w.k_end - key0);
           const int n_v = (valid + kVKeys - 1) / kVKeys;
-          const uint32_t xb = smem_u32(xbuf + (gj % kXBufs) * kXBytes);
           const uint32_t idesc_pv = instr_desc(E::kFmt, 2 * kRows, nn, false, true);
+          // P pieces of this tile: uses 2 gj (keys 0..63) and 2 gj + 1 (64..127).  Each is
+          // waited for before its first V stage (both always, so every slot phase is
+          // consumed) and, when the slot's next use belongs to this item, handed back to the
+          // D-peer pair by a commit once the P.V instructions reading it complete.
+          int pc_ready = -1;
+          auto take_piece = [&](int pc) -> bool {
+            const int u = 2 * gj + pc;
+            if (!mbar_wait<true>(smem_u32(&bars.p_full[u % kXSlots]), static_cast<uint32_t>(u / kXSlots) & 1u,
+                                 kTimeoutSoftmax, abort))
+              return false;
+            tc_fence_after();
+            pc_ready = pc;
+            return true;
+          };
+          auto give_piece = [&](int pc) {
+            const int u = 2 * gj + pc;
+            if (u + kXSlots < u_end) mma_commit_pair_mc(smem_u32(&bars.x_empty[u % kXSlots]), peer_mask);
+          };
+          if (!(ok = take_piece(0))) break;
+          XATTN_TRACE_POINT(4, j);
           for (int v = 0; v < n_v; ++v) {
+            const int pc = v * kVKeys / kGroupCols;  // piece of this stage's keys
+            if (pc > pc_ready && !(ok = take_piece(pc))) break;
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
             tc_fence_after();
             const uint32_t st = smem_u32(stages + s * kStageBytes);
+            const uint32_t xb = smem_u32(xbuf) + ((2 * gj + pc) % kXSlots) * kPieceBytes;
             const int ksteps = min(kVKeys / E::kKStep, (valid - v * kVKeys + E::kKStep - 1) / E::kKStep);
             for (int kk = 0; kk < ksteps; ++kk) {
-              const int key = v * kVKeys + kk * E::kKStep;
+              const int key = v * kVKeys + kk * E::kKStep - pc * kGroupCols;  // key within the piece
               // P: K-major, kCols keys per 128-byte row, 16 KB per key group
               const uint64_t ad = smem_desc(xb + (key / E::kCols) * 16384 + (key % E::kCols) * sizeof(T),
                                             16, 1024, kSw128);
@@ -392,9 +425,14 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             }
             mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
             if (++s == kStages) { s = 0; phase ^= 1u; }
+            if (v == n_v - 1 || (v + 1) * kVKeys % kGroupCols == 0) give_piece(pc);
           }
           if (!ok) break;
-          mma_commit_pair_mc(smem_u32(&bars.pv_done[gj % kXBufs]), pair_mask);
+          // a piece without valid keys (short last tile) still completes its phases
+          for (int pc = pc_ready + 1; pc < kGroups && ok; ++pc)
+            if ((ok = take_piece(pc))) give_piece(pc);
+          if (!ok) break;
+          mma_commit_pair_mc(smem_u32(&bars.pv_done[gj & 1]), pair_mask);
           XATTN_TRACE_POINT(5, j);
         }
         if (!ok) break;
@@ -412,31 +450,38 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     const int grp = sw >> 2;
     const int row = quad * 32 + lane;
     const int cbase = grp * kGroupCols;
-    const int ch0 = cbase / 4;
     const uint32_t t_row = tmem + (static_cast<uint32_t>(quad * 32) << 16);
     const uint32_t peer_x_row0 = mapa_shared(smem_u32(xbuf) + x_offset(0, row), dpeer);
     const uint32_t peer_x_full0 = mapa_shared(smem_u32(&bars.x_full[0]), dpeer);
-    const uint32_t peer_x_empty = mapa_shared(smem_u32(&bars.x_empty), dpeer);
+    const uint32_t peer_x_empty0 = mapa_shared(smem_u32(&bars.x_empty[0]), dpeer);
     const uint32_t lead_s_free = mapa_shared(smem_u32(&bars.s_free), leader);
     const uint32_t lead_p_full0 = mapa_shared(smem_u32(&bars.p_full[0]), leader);
-    const bool arm_thread = (sw == 0 && lane == 0);
+    const bool arm_thread = ((sw & 3) == 0 && lane == 0);  // one per group
 
     bool ok = true;
     int g = 0;   // global index of the item's first tile
     int it = 0;  // items with tiles done
-    // Exchange permissions: the tiles of the cluster's first item with tiles, at most two,
-    // find both of the D-peer's buffers free; every later tile t waits for the peer's
-    // release (phase t - n_impl of x_empty).  (A later item's first tile can be global tile
-    // 1 when the first item has a single tile: it must wait too, since the peer's epilogue
-    // stages the output in these buffers.)
-    int n_impl = 0;
+    // Exchange permissions.  My group sends piece use u = 2 g + grp into the D-peer's slot
+    // u % 3.  The uses of the cluster's first item with tiles below n_free (3, or 2 when that
+    // item has one tile: the third slot then first holds the peer's epilogue staging) find
+    // their slots free; every later use waits for the release of use u - 3 of the slot.
+    // Releases come, in use order per slot, from the D-peer pair leader's commit after the
+    // P.V that read the piece when use u + 3 belongs to the same item, else from the D-peer
+    // after the epilogue that precedes use u + 3 (it stages the output in every slot).
+    int n_free = 0;
     for (int i2 = cid; i2 < p.n_items; i2 += n_clusters) {
       const int nt = item_at(i2).n_tiles;
       if (nt > 0) {
-        n_impl = min(kXBufs, nt);
+        n_free = min(kXSlots, 2 * nt);
         break;
       }
     }
+    // phase of slot (u % 3)'s x_empty that use u >= n_free waits for: releases of the slot
+    // counted from its first use at or above n_free
+    auto x_empty_parity = [&](int u) -> uint32_t {
+      const int first = n_free + ((u - n_free) % kXSlots + kXSlots) % kXSlots;
+      return static_cast<uint32_t>((u - first) / kXSlots) & 1u;
+    };
     for (int item = cid; item < p.n_items; item += n_clusters) {
       const Item w = item_at(item);
       const int b = w.b, split = w.split, row0 = w.row0;
@@ -447,12 +492,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       const int gj = g + j;  // global tile index
       const int key0 = w.k_begin + j * kKeys;
       const int valid = min(kKeys, w.k_end - key0);
-      // buffer of tile gj: gj % kXBufs, used for the (gj / kXBufs)-th time
-      const int xb_i = gj % kXBufs;
-      const uint32_t xb_par = static_cast<uint32_t>(gj / kXBufs) & 1u;
-      uint8_t* xcur = xbuf + xb_i * kXBytes;
-      const uint32_t peer_x_row = peer_x_row0 + xb_i * kXBytes;
-      const uint32_t peer_x_full = peer_x_full0 + xb_i * 8;
+      // my group's piece of tile gj: use u, slot u % 3, used for the (u / 3)-th time
+      const int u = 2 * gj + grp;
+      const int slot = u % kXSlots;
+      const uint32_t x_par = static_cast<uint32_t>(u / kXSlots) & 1u;
+      uint8_t* xcur = xbuf + slot * kPieceBytes;
+      const uint32_t peer_x_row = peer_x_row0 + slot * kPieceBytes;
+      const uint32_t peer_x_full = peer_x_full0 + slot * 8;
       // After a failed bounded wait a warp keeps iterating with the work skipped (later waits
       // fail at once through the abort flag), so every softmax warp reaches each named
       // barrier equally often and none is left in bar.sync.
@@ -471,30 +517,30 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_remote(lead_s_free);
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
       }
-      // the D-peer's buffer gj % 2 is free for this tile once it signalled so (gj >= n_impl)
-      if (ok && gj >= n_impl)
-        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty), (gj - n_impl) & 1, kTimeoutExchange, abort);
+      // the D-peer's slot is free for this use once released (u >= n_free)
+      if (ok && u >= n_free)
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty[slot]), x_empty_parity(u), kTimeoutExchange, abort);
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_async_v4(peer_x_row + (ch0 + i) * (kRows * 16), peer_x_full, __uint_as_float(ra[4 * i]),
+          st_async_v4(peer_x_row + i * (kRows * 16), peer_x_full, __uint_as_float(ra[4 * i]),
                       __uint_as_float(ra[4 * i + 1]), __uint_as_float(ra[4 * i + 2]),
                       __uint_as_float(ra[4 * i + 3]));
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_async_v4(peer_x_row + (ch0 + 8 + i) * (kRows * 16), peer_x_full,
+          st_async_v4(peer_x_row + (8 + i) * (kRows * 16), peer_x_full,
                       __uint_as_float(rb[4 * i]), __uint_as_float(rb[4 * i + 1]),
                       __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
-        if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[xb_i]), kXBytes);
+        if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[slot]), kPieceBytes);
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
-        ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[xb_i]), xb_par, kTimeoutPeer, abort);
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[slot]), x_par, kTimeoutPeer, abort);
       }
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(ch0 + i, row));
+          const float4 o = *reinterpret_cast<const float4*>(xcur + x_offset(i, row));
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int key = cbase + 4 * i + e;
@@ -524,8 +570,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         m_run = tmax;
       }
       if (__any_sync(0xffffffffu, alpha != 1.f)) {
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(gj - 1) % kXBufs]),
-                                  static_cast<uint32_t>((gj - 1) / kXBufs) & 1u, kTimeoutMmaDone,
+        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(gj - 1) & 1]),
+                                  static_cast<uint32_t>((gj - 1) >> 1) & 1u, kTimeoutMmaDone,
                                   abort)))
           continue;
         tc_fence_after();
@@ -551,7 +597,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
             lsum += __uint_as_float(q4[e]);
           }
-          *reinterpret_cast<uint4*>(xcur + p_offset(ch0 + i, row)) =
+          *reinterpret_cast<uint4*>(xcur + p_offset(i, row)) =
               make_uint4(q4[0], q4[1], q4[2], q4[3]);
         }
       } else {
@@ -570,7 +616,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             lsum += back.x + back.y;
             h4[e] = *reinterpret_cast<const uint32_t*>(&hv);
           }
-          *reinterpret_cast<uint4*>(xcur + grp * 16384 + row * 128 + ((c ^ (row & 7)) << 4)) =
+          *reinterpret_cast<uint4*>(xcur + row * 128 + ((c ^ (row & 7)) << 4)) =
               make_uint4(h4[0], h4[1], h4[2], h4[3]);
         }
       }
@@ -580,23 +626,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(17, j);
-      if (lane == 0) mbar_arrive_remote(lead_p_full0 + xb_i * 8);
+      if (lane == 0) mbar_arrive_remote(lead_p_full0 + slot * 8);
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
-      if (gj >= 1 && j + 1 < w.n_tiles) {
-        // my buffer (gj+1) % 2 held P of tile gj-1; once that P.V completed the D-peer may
-        // send tile gj+1 into it.  Every global tile t >= n_impl is released exactly once:
-        // here by the end of tile t-1 of the same item (then t >= 2 >= n_impl), or after the
-        // previous item's epilogue (which stages the output in these buffers) for an item's
-        // first tile.  Consecutive
-        // releases from one warp are separated by the all-warp barrier of a tile, so no
-        // warp's arrival counts toward another release's phase.
-        if (!(ok = warp_mbar_wait(smem_u32(&bars.pv_done[(gj + 1) % kXBufs]),
-                                  static_cast<uint32_t>((gj - 1) / kXBufs) & 1u, kTimeoutMmaDone,
-                                  abort)))
-          continue;
-        if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, j);
-        if (lane == 0) mbar_arrive_remote(peer_x_empty);
-      }
     }
     // ---- epilogue of the item
     red[grp][row] = l_run;
@@ -623,16 +654,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         scale = p.out_comp / l_tot;
       }
       // o_done (a multicast commit after the item's last P.V) means every P.V of the item
-      // completed, so both exchange buffers are free (the ring already holds the next
-      // item's operands): 16 KB of staging per softmax warp, O stored in rounds
-      fused::store_o_tma(&p.to, p.split_mode != 0, smem_u32(xbuf) + sw * (kXBufs * kXBytes / (kSoftmaxThreads / 32)),
-                         kXBufs * kXBytes / (kSoftmaxThreads / 32) / 4096, t_row, dh, grp, lane, scale,
-                         col0, split, row0 + quad * 32, b, row0 + quad * 32 < p.n_latent);
+      // completed and no slot holds a pending piece (the D-peer sends the next item's pieces
+      // only after the releases below; the ring already holds the next item's operands):
+      // the slots stage O, kStagePerWarp bytes per softmax warp, stored in rounds
+      fused::store_o_tma(&p.to, p.split_mode != 0, smem_u32(xbuf) + sw * kStagePerWarp,
+                         kStagePerWarp / 4096, t_row, dh, grp, lane, scale, col0, split,
+                         row0 + quad * 32, b, row0 + quad * 32 < p.n_latent);
       tc_fence_before();
-      // the staging has been read: the D-peer may send the next item's first tile into my
-      // buffer (g + n_tiles) % 2, whose last P.V (tile g + n_tiles - 2) is complete
-      if (g + w.n_tiles >= n_impl && item + n_clusters < p.n_items && lane == 0)
-        mbar_arrive_remote(peer_x_empty);
     } else if (w.n_tiles == 0 && p.split_mode && live) {
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
       float* dst = p.po + pidx * p.dim + col0;
@@ -643,6 +671,21 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
     if (w.n_tiles > 0) {
+      // Every warp's staging has been read by its TMA stores: hand the slots whose next use
+      // follows this epilogue back to the D-peer, uses u in [u1 - 3, u1n - 3) below u1 (u1,
+      // u1n: first piece uses of the next and the one after; a use whose successor lies
+      // past a one-tile next item is handed back after that item's epilogue instead).
+      int nt_next = 0;
+      for (int i2 = item + n_clusters; i2 < p.n_items && nt_next == 0; i2 += n_clusters)
+        nt_next = item_at(i2).n_tiles;
+      if (nt_next > 0) {
+        named_bar_sync(1, kSoftmaxThreads);
+        if (sw == 0 && lane == 0) {
+          const int u1 = 2 * (g + w.n_tiles), u1n = u1 + 2 * nt_next;
+          for (int uu = max(u1 - kXSlots, n_free - kXSlots); uu < min(u1, u1n - kXSlots); ++uu)
+            mbar_arrive_remote(peer_x_empty0 + ((uu % kXSlots + kXSlots) % kXSlots) * 8);
+        }
+      }
       g += w.n_tiles;
       ++it;
     }
