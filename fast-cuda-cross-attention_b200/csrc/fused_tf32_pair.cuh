@@ -640,6 +640,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     const bool live = grow < p.n_latent;
     if (ok && w.n_tiles > 0 &&
         (ok = warp_mbar_wait(smem_u32(&bars.o_done), it & 1, kTimeoutMmaDone, abort))) {
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, it);
       tc_fence_after();
       float scale;
       if (p.split_mode) {
@@ -678,6 +679,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       int nt_next = 0;
       for (int i2 = item + n_clusters; i2 < p.n_items && nt_next == 0; i2 += n_clusters)
         nt_next = item_at(i2).n_tiles;
+      if (sw == 0 && lane == 0) XATTN_TRACE_POINT(20, it);
       if (nt_next > 0) {
         named_bar_sync(1, kSoftmaxThreads);
         if (sw == 0 && lane == 0) {
