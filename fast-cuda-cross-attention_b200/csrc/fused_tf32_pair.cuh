@@ -202,6 +202,11 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     w.n_tiles = w.k_end > w.k_begin ? (w.k_end - w.k_begin + kKeys - 1) / kKeys : 0;
     return w;
   };
+  // the cluster's next item with key tiles at or after `item` (p.n_items if none)
+  auto with_tiles = [&](int item) {
+    while (item < p.n_items && item_at(item).n_tiles == 0) item += n_clusters;
+    return item;
+  };
   const int dh = p.dh;
   const int n_qk_chunks = dh / E::kCols;
   const int col0 = static_cast<int>(h) * dh;
@@ -371,7 +376,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         mma_qk(0);
-        const int u_end = 2 * (g + w.n_tiles);  // first piece use of the cluster's next item
+        const int u_end = 2 * (g + w.n_tiles);  // one past the item's last piece use
         for (int j = 0; j < w.n_tiles && ok; ++j) {
           const int gj = g + j;
           if (j + 1 < w.n_tiles) {
@@ -386,8 +391,9 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t idesc_pv = instr_desc(E::kFmt, 2 * kRows, nn, false, true);
           // P pieces of this tile: uses 2 gj (keys 0..63) and 2 gj + 1 (64..127).  Each is
           // waited for before its first V stage (both always, so every slot phase is
-          // consumed) and, when the slot's next use belongs to this item, handed back to the
-          // D-peer pair by a commit once the P.V instructions reading it complete.
+          // consumed) and handed back to the D-peer pair by a commit once the P.V
+          // instructions reading it complete -- except the item's last piece, whose slot
+          // stages the epilogue's output and is handed back after it.
           int pc_ready = -1;
           auto take_piece = [&](int pc) -> bool {
             const int u = 2 * gj + pc;
@@ -400,7 +406,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           };
           auto give_piece = [&](int pc) {
             const int u = 2 * gj + pc;
-            if (u + kXSlots < u_end) mma_commit_pair_mc(smem_u32(&bars.x_empty[u % kXSlots]), peer_mask);
+            if (u != u_end - 1) mma_commit_pair_mc(smem_u32(&bars.x_empty[u % kXSlots]), peer_mask);
           };
           if (!(ok = take_piece(0))) break;
           XATTN_TRACE_POINT(4, j);
@@ -462,26 +468,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     int g = 0;   // global index of the item's first tile
     int it = 0;  // items with tiles done
     // Exchange permissions.  My group sends piece use u = 2 g + grp into the D-peer's slot
-    // u % 3.  The uses of the cluster's first item with tiles below n_free (3, or 2 when that
-    // item has one tile: the third slot then first holds the peer's epilogue staging) find
-    // their slots free; every later use waits for the release of use u - 3 of the slot.
-    // Releases come, in use order per slot, from the D-peer pair leader's commit after the
-    // P.V that read the piece when use u + 3 belongs to the same item, else from the D-peer
-    // after the epilogue that precedes use u + 3 (it stages the output in every slot).
-    int n_free = 0;
-    for (int i2 = cid; i2 < p.n_items; i2 += n_clusters) {
-      const int nt = item_at(i2).n_tiles;
-      if (nt > 0) {
-        n_free = min(kXSlots, 2 * nt);
-        break;
-      }
-    }
-    // phase of slot (u % 3)'s x_empty that use u >= n_free waits for: releases of the slot
-    // counted from its first use at or above n_free
-    auto x_empty_parity = [&](int u) -> uint32_t {
-      const int first = n_free + ((u - n_free) % kXSlots + kXSlots) % kXSlots;
-      return static_cast<uint32_t>((u - first) / kXSlots) & 1u;
-    };
+    // u % 3.  Uses 0..2 find their slots free; use u >= 3 waits for the release of use u - 3
+    // of its slot (phase u / 3 - 1 of x_empty[u % 3]).  Releases come, in use order per
+    // slot, from the D-peer pair leader's commit after the P.V that read the piece, or, for
+    // the last piece of an item, from the D-peer after that item's epilogue, which stages
+    // the output in that piece's slot (the next item's first pieces go to the other two
+    // slots, so they cross while the epilogue runs).
+    auto x_empty_parity = [&](int u) -> uint32_t { return static_cast<uint32_t>(u / kXSlots - 1) & 1u; };
     for (int item = cid; item < p.n_items; item += n_clusters) {
       const Item w = item_at(item);
       const int b = w.b, split = w.split, row0 = w.row0;
@@ -517,8 +510,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive_remote(lead_s_free);
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(19, j);
       }
-      // the D-peer's slot is free for this use once released (u >= n_free)
-      if (ok && u >= n_free)
+      // the D-peer's slot is free for this use once released (u >= 3)
+      if (ok && u >= kXSlots)
         ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty[slot]), x_empty_parity(u), kTimeoutExchange, abort);
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(12, j);
@@ -655,12 +648,16 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         scale = p.out_comp / l_tot;
       }
       // o_done (a multicast commit after the item's last P.V) means every P.V of the item
-      // completed and no slot holds a pending piece (the D-peer sends the next item's pieces
-      // only after the releases below; the ring already holds the next item's operands):
-      // the slots stage O, kStagePerWarp bytes per softmax warp, stored in rounds
-      fused::store_o_tma(&p.to, p.split_mode != 0, smem_u32(xbuf) + sw * kStagePerWarp,
-                         kStagePerWarp / 4096, t_row, dh, grp, lane, scale, col0, split,
-                         row0 + quad * 32, b, row0 + quad * 32 < p.n_latent);
+      // completed: the slot of the item's last piece, which the D-peer refills only after
+      // the release below, stages O, a 4 KB box per softmax warp
+      const int y0 = row0 + quad * 32;
+      const size_t rs = p.split_mode ? static_cast<size_t>(p.num_splits) * p.dim : p.dim;
+      float* dst0 = p.split_mode
+                        ? p.po + ((static_cast<size_t>(b) * p.n_latent + y0) * p.num_splits + split) * p.dim + col0
+                        : p.out + (static_cast<size_t>(b) * p.n_latent + y0) * p.dim + col0;
+      const uint32_t stage = smem_u32(xbuf) + ((2 * (g + w.n_tiles) - 1) % kXSlots) * kPieceBytes;
+      fused::store_o_direct(dst0, rs, stage + sw * 4096, t_row, dh, grp, lane, scale,
+                            min(32, p.n_latent - y0));
       tc_fence_before();
     } else if (w.n_tiles == 0 && p.split_mode && live) {
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
@@ -672,21 +669,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       }
     }
     if (w.n_tiles > 0) {
-      // Every warp's staging has been read by its TMA stores: hand the slots whose next use
-      // follows this epilogue back to the D-peer, uses u in [u1 - 3, u1n - 3) below u1 (u1,
-      // u1n: first piece uses of the next and the one after; a use whose successor lies
-      // past a one-tile next item is handed back after that item's epilogue instead).
-      int nt_next = 0;
-      for (int i2 = item + n_clusters; i2 < p.n_items && nt_next == 0; i2 += n_clusters)
-        nt_next = item_at(i2).n_tiles;
+      // Every warp has read its staging box back: hand the slot of the item's last piece
+      // back to the D-peer (if the cluster has further tiles).
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(20, it);
-      if (nt_next > 0) {
+      if (with_tiles(item + n_clusters) < p.n_items) {
         named_bar_sync(1, kSoftmaxThreads);
-        if (sw == 0 && lane == 0) {
-          const int u1 = 2 * (g + w.n_tiles), u1n = u1 + 2 * nt_next;
-          for (int uu = max(u1 - kXSlots, n_free - kXSlots); uu < min(u1, u1n - kXSlots); ++uu)
-            mbar_arrive_remote(peer_x_empty0 + ((uu % kXSlots + kXSlots) % kXSlots) * 8);
-        }
+        if (sw == 0 && lane == 0)
+          mbar_arrive_remote(peer_x_empty0 + ((2 * (g + w.n_tiles) - 1) % kXSlots) * 8);
       }
       g += w.n_tiles;
       ++it;
