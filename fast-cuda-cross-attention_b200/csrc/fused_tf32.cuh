@@ -86,6 +86,8 @@ struct Params {
   CUtensorMap tq;   // Q [B][Nl][D] fp32, box {32, 128, 1}, 128B swizzle
   CUtensorMap tk;   // K [B][Ni][D] fp32, box {32, 128, 1}, 128B swizzle
   CUtensorMap tv;   // V [B][Ni][D] fp32, box {32, 16, 1}, 128B swizzle / 32B atoms
+  CUtensorMap tk8;  // K [B][Ni][D], box {one 128-byte row of columns, 8 keys, 1} (pair
+                    // kernel: the short remainder of a key range folded into its first tile)
   CUtensorMap to;   // output: out {D, Nl, B} box {32, 32, 1}, or po {D, S, Nl, B} box
                     // {32, 1, 32, 1} in split mode; 128B swizzle
   float* out;       // [B][Nl][D]                      (final mode)
@@ -218,9 +220,11 @@ __device__ __forceinline__ float4 ld_shared_f4(uint32_t addr) {
 //   dst0        output address of this warp's first row at the CTA's first column
 //   row_stride  floats between consecutive output rows
 //   rows_valid  rows of this warp that exist (<= 0: none)
+//   first_read  a cluster mbarrier that lane 0 arrives on once the first chunk has left
+//               TMEM (0: none)
 __device__ __forceinline__ void store_o_direct(float* dst0, size_t row_stride, uint32_t box,
                                                uint32_t t_row, int dh, int grp, int lane,
-                                               float scale, int rows_valid) {
+                                               float scale, int rows_valid, uint32_t first_read = 0) {
   const int n = (dh / 32 - grp + kGroups - 1) / kGroups;  // chunks of this warp
   const int q = lane & 7;
   auto put = [&](const uint32_t (&o)[32], int i) {
@@ -245,6 +249,11 @@ __device__ __forceinline__ void store_o_direct(float* dst0, size_t row_stride, u
     uint32_t o[32];
     tmem_ld32(t_row + (grp + i * kGroups) * 32, o);
     tmem_ld_wait();
+    if (i == 0 && first_read != 0) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(first_read);
+    }
     put(o, i);
   }
 }

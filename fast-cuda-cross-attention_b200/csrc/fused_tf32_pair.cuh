@@ -126,14 +126,22 @@ constexpr int kThreads = 64 + kSoftmaxThreads + 32 * (kProducers - 1);
 // already required stage i - kProducers <= i - kStages to be consumed.
 static_assert(kProducers <= kStages, "parity-only empty waits need kProducers <= kStages");
 constexpr int kXRegion = kXSlots * kPieceBytes;
-constexpr int kSmemBytes = kStages * kStageBytes + kXRegion + 1024;
+// Folded remainder: a key range whose last 1..kFold keys would form a short last tile (the
+// 16 keys of N_input = 784) adds them to its first tile instead: an N = 16 Q.K^T into TMEM
+// columns 0..15 (O's columns, free until that tile's P.V), an extra exchange piece (8 KB
+// of a slot) and an extra V stage.  A short tile costs a whole pass over Q.
+constexpr int kFold = 16;
+constexpr int kKxBytes = 1024;       // per stage: 8 keys x one 128-byte row of the folded K
+constexpr int kSmemBytes = kStages * kStageBytes + kXRegion + kStages * kKxBytes + 1024;
 constexpr int kStaticSmemBytes = 2048;
 static_assert(kSmemBytes + kStaticSmemBytes <= 232448, "exceeds 227 KB of shared memory per CTA");
 // Output staging: the exchange slots, split evenly between the softmax warps in 4 KB boxes.
 constexpr int kStagePerWarp = kXRegion / (kSoftmaxThreads / 32);
 static_assert(kStagePerWarp % 4096 == 0 && kStagePerWarp >= 4096, "output staging boxes");
 constexpr int kSoftmaxWarpsPerPair = 2 * kSoftmaxThreads / 32;
-constexpr int kPieceWarpsPerPair = kSoftmaxWarpsPerPair / kGroups;  // writers of one P piece
+// P pieces complete after kSoftmaxWarpsPerPair arrivals: a group's piece by its warps with
+// a count of kGroups each, the folded piece (written by every warp) with a count of one
+constexpr uint32_t kPieceArrivals = kSoftmaxWarpsPerPair;
 
 // D halves this kernel takes: one pair instruction covers N = dh (dh <= 256) or two of
 // N = dh / 2 (dh = 384); each CTA holds N / 2 columns of V per instruction, whole 32-wide
@@ -154,6 +162,8 @@ struct __align__(8) Barriers {
   uint64_t x_empty[kXSlots]; // the D-peer's slot b may be refilled: one arrival per release,
                              // by the D-peer pair leader's commit after P.V read the piece, or
                              // by the D-peer after an epilogue that staged O in its slots
+  uint64_t o_lo_read;        // leader: both CTAs' epilogues read O's first 32 columns (a
+                             // folded Q.K^T of the next item writes columns 0..15)
   uint64_t drain;            // leader: its MMAs completed
 };
 
@@ -167,6 +177,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* stages = smem;
   uint8_t* xbuf = smem + kStages * kStageBytes;
+  uint8_t* kxbuf = xbuf + kXRegion;  // folded K rows, one kKxBytes box per ring slot
   __shared__ Barriers bars;
   __shared__ float red[kGroups][kRows];
   __shared__ uint32_t tmem_slot;
@@ -190,6 +201,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   const int n_rb2 = (p.n_latent + 2 * kRows - 1) / (2 * kRows);
   struct Item {
     int b, split, row0, k_begin, k_end, n_tiles;
+    int extra;  // keys folded into the first tile (the last `extra` keys of the range)
+    __device__ int uses() const { return 2 * n_tiles + (extra > 0); }  // exchange pieces
   };
   auto item_at = [&](int item) {
     Item w;
@@ -199,7 +212,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     w.row0 = rb2 * 2 * kRows + static_cast<int>(r) * kRows;  // this CTA's rows
     w.k_begin = w.split * p.split_chunk;
     w.k_end = min(w.k_begin + p.split_chunk, p.n_input);
-    w.n_tiles = w.k_end > w.k_begin ? (w.k_end - w.k_begin + kKeys - 1) / kKeys : 0;
+    const int nk = w.k_end - w.k_begin;
+    w.n_tiles = nk > 0 ? (nk + kKeys - 1) / kKeys : 0;
+    w.extra = 0;
+    if (nk > kKeys && nk % kKeys != 0 && nk % kKeys <= kFold) {
+      w.extra = nk % kKeys;
+      --w.n_tiles;
+    }
     return w;
   };
   // the cluster's next item with key tiles at or after `item` (p.n_items if none)
@@ -225,12 +244,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&bars.s_full), 1);
     mbar_init(smem_u32(&bars.s_free), kSoftmaxWarpsPerPair);
     for (int i = 0; i < kXSlots; ++i) {
-      mbar_init(smem_u32(&bars.p_full[i]), kPieceWarpsPerPair);
+      mbar_init(smem_u32(&bars.p_full[i]), kPieceArrivals);
       mbar_init(smem_u32(&bars.x_full[i]), 1);
       mbar_init(smem_u32(&bars.x_empty[i]), 1);
     }
     for (int i = 0; i < 2; ++i) mbar_init(smem_u32(&bars.pv_done[i]), 1);
     mbar_init(smem_u32(&bars.o_done), 1);
+    mbar_init(smem_u32(&bars.o_lo_read), kSoftmaxWarpsPerPair / kGroups);
     mbar_init(smem_u32(&bars.drain), 1);
     fence_mbar_init();
   }
@@ -242,6 +262,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&p.tq);
     tma_prefetch_desc(&p.tk);
     tma_prefetch_desc(&p.tv);
+    tma_prefetch_desc(&p.tk8);
   }
   tc_fence_before();
   cluster_sync();
@@ -291,11 +312,16 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
                 tma_prefetch_4d(&p.tv, 0, key0 + v * kVKeys,
                                 (col0 + n * nn + static_cast<int>(r) * (nn / 2)) / E::kCols, w.b);
           }
+          const bool fold = j == 0 && w.extra > 0;
+          const int xbase = w.k_begin + w.n_tiles * kKeys + static_cast<int>(r) * (kFold / 2);
           for (int c = 0; c < n_qk_chunks && ok; ++c, ++i) {
-            if (!own(16384 + 8192)) continue;
+            if (!own(16384 + 8192 + (fold ? kKxBytes : 0))) continue;
             const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
             tma_load_3d_pair(st, &p.tq, fb, col0 + c * E::kCols, w.row0, w.b);
             tma_load_3d_pair(st + 16384, &p.tk, fb, col0 + c * E::kCols, kbase, w.b);
+            if (fold)  // this CTA's half of the folded keys (rows past the range read as zero or are masked)
+              tma_load_3d_pair(smem_u32(kxbuf + (i % kStages) * kKxBytes), &p.tk8, fb,
+                               col0 + c * E::kCols, xbase, w.b);
             // and the same chunk of the next tile's keys (out-of-range boxes prefetch nothing)
             if (j + 1 < w.n_tiles)
               tma_prefetch_3d(&p.tk, col0 + c * E::kCols, key0 + kKeys + static_cast<int>(r) * (kKeys / 2), w.b);
@@ -306,15 +332,17 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           const int valid = min(kKeys, w.k_end - key0);
           const int n_v = (valid + kVKeys - 1) / kVKeys;
           if (pid == 0) XATTN_TRACE_POINT(1, j);
-          for (int v = 0; v < n_v && ok; ++v, ++i) {
+          // the tile's V stages, then (first tile of a folded range) one stage at the folded keys
+          const int n_vx = n_v + (j == 0 && w.extra > 0 ? 1 : 0);
+          for (int v = 0; v < n_vx && ok; ++v, ++i) {
             if (!own(n_slabs * kVKeys * 128)) continue;
             const uint32_t st = smem_u32(stages + (i % kStages) * kStageBytes);
+            const int vkey = v < n_v ? key0 + v * kVKeys : w.k_begin + w.n_tiles * kKeys;
             // one box of spi slabs per instruction: slab index (dim / kCols) is the tensor
             // map's third coordinate
             for (int n = 0; n < n_instr; ++n) {
               const int dim = col0 + n * nn + static_cast<int>(r) * (nn / 2);
-              tma_load_4d_pair(st + n * spi * (kVKeys * 128), &p.tv, fb, 0, key0 + v * kVKeys,
-                               dim / E::kCols, w.b);
+              tma_load_4d_pair(st + n * spi * (kVKeys * 128), &p.tv, fb, 0, vkey, dim / E::kCols, w.b);
             }
           }
         };
@@ -340,6 +368,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int g = 0;  // global index of the item's first tile
+      int U = 0;  // piece use of the item's first piece
+      int n_lo = 0;  // o_lo_read phases waited for
       const uint32_t t_s = tmem + kSCol;
       const uint16_t peer_mask = static_cast<uint16_t>(3u << (leader ^ 2u));  // the D-peer pair
       for (int item = cid; item < p.n_items && ok; item += n_clusters) {
@@ -350,6 +380,17 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           const int valid = min(kKeys, w.k_end - key0);
           const int n_qk = (valid + 15) & ~15;
           const uint32_t idesc = instr_desc(E::kFmt, 2 * kRows, n_qk, false, false);
+          // folded keys: N = 16 into TMEM columns 0..15, which the previous item's epilogue
+          // must have read first
+          const bool fold = j == 0 && w.extra > 0;
+          const uint32_t idesc_x = instr_desc(E::kFmt, 2 * kRows, kFold, false, false);
+          if (fold && g > 0) {
+            if (!(ok = mbar_wait<true>(smem_u32(&bars.o_lo_read), static_cast<uint32_t>(n_lo) & 1u,
+                                       kTimeoutSoftmax, abort)))
+              return;
+            ++n_lo;
+            tc_fence_after();
+          }
           for (int c = 0; c < n_qk_chunks && ok; ++c) {
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
             if (c == 0) XATTN_TRACE_POINT(2, j);
@@ -360,6 +401,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
               const uint64_t ad = smem_desc(st + kk * 32, 16, 1024, kSw128);
               const uint64_t bd = smem_desc(st + 16384 + kk * 32, 16, 1024, kSw128);
               mma_pair<T>(t_s, ad, bd, idesc, (c | kk) != 0);
+            }
+            if (fold) {
+              const uint32_t kx = smem_u32(kxbuf + s * kKxBytes);
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_pair<T>(tmem, smem_desc(st + kk * 32, 16, 1024, kSw128),
+                            smem_desc(kx + kk * 32, 16, 1024, kSw128), idesc_x, (c | kk) != 0);
             }
             mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
             if (++s == kStages) { s = 0; phase ^= 1u; }
@@ -376,9 +424,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           tc_fence_after();
         }
         mma_qk(0);
-        const int u_end = 2 * (g + w.n_tiles);  // one past the item's last piece use
+        if (!ok) break;
+        const int u_end = U + w.uses();  // one past the item's last piece use
         for (int j = 0; j < w.n_tiles && ok; ++j) {
           const int gj = g + j;
+          const bool fold = j == 0 && w.extra > 0;
+          const int u0 = U + 2 * j + (j > 0 && w.extra > 0 ? 1 : 0);  // the tile's first piece
           if (j + 1 < w.n_tiles) {
             if (!(ok = mbar_wait<true>(smem_u32(&bars.s_free), gj & 1, kTimeoutSoftmax, abort))) break;
             tc_fence_after();
@@ -389,14 +440,15 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           const int valid = min(kKeys, w.k_end - key0);
           const int n_v = (valid + kVKeys - 1) / kVKeys;
           const uint32_t idesc_pv = instr_desc(E::kFmt, 2 * kRows, nn, false, true);
-          // P pieces of this tile: uses 2 gj (keys 0..63) and 2 gj + 1 (64..127).  Each is
-          // waited for before its first V stage (both always, so every slot phase is
-          // consumed) and handed back to the D-peer pair by a commit once the P.V
-          // instructions reading it complete -- except the item's last piece, whose slot
-          // stages the epilogue's output and is handed back after it.
+          // P pieces of this tile: uses u0 (keys 0..63), u0 + 1 (64..127) and, for the first
+          // tile of a folded range, u0 + 2 (the folded keys).  Each is waited for before its
+          // first V stage (all of them always, so every slot phase is consumed) and handed
+          // back to the D-peer pair by a commit once the P.V instructions reading it complete
+          // -- except the item's last piece, whose slot stages the epilogue's output and is
+          // handed back after it.
           int pc_ready = -1;
           auto take_piece = [&](int pc) -> bool {
-            const int u = 2 * gj + pc;
+            const int u = u0 + pc;
             if (!mbar_wait<true>(smem_u32(&bars.p_full[u % kXSlots]), static_cast<uint32_t>(u / kXSlots) & 1u,
                                  kTimeoutSoftmax, abort))
               return false;
@@ -405,7 +457,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             return true;
           };
           auto give_piece = [&](int pc) {
-            const int u = 2 * gj + pc;
+            const int u = u0 + pc;
             if (u != u_end - 1) mma_commit_pair_mc(smem_u32(&bars.x_empty[u % kXSlots]), peer_mask);
           };
           if (!(ok = take_piece(0))) break;
@@ -416,7 +468,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
             tc_fence_after();
             const uint32_t st = smem_u32(stages + s * kStageBytes);
-            const uint32_t xb = smem_u32(xbuf) + ((2 * gj + pc) % kXSlots) * kPieceBytes;
+            const uint32_t xb = smem_u32(xbuf) + ((u0 + pc) % kXSlots) * kPieceBytes;
             const int ksteps = min(kVKeys / E::kKStep, (valid - v * kVKeys + E::kKStep - 1) / E::kKStep);
             for (int kk = 0; kk < ksteps; ++kk) {
               const int key = v * kVKeys + kk * E::kKStep - pc * kGroupCols;  // key within the piece
@@ -438,12 +490,32 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           for (int pc = pc_ready + 1; pc < kGroups && ok; ++pc)
             if ((ok = take_piece(pc))) give_piece(pc);
           if (!ok) break;
+          if (fold) {
+            // the folded keys: P piece u0 + 2 (P at 16 KB into its slot), one V stage
+            if (!(ok = take_piece(kGroups))) break;
+            if (!(ok = mbar_wait(smem_u32(&bars.full[s]), phase, kTimeoutTmaFull, abort))) break;
+            tc_fence_after();
+            const uint32_t st = smem_u32(stages + s * kStageBytes);
+            const uint32_t xb = smem_u32(xbuf) + ((u0 + kGroups) % kXSlots) * kPieceBytes + 16384;
+            for (int kk = 0; kk * E::kKStep < w.extra; ++kk) {
+              const uint64_t ad = smem_desc(xb + kk * E::kKStep * sizeof(T), 16, 1024, kSw128);
+              for (int n = 0; n < n_instr; ++n) {
+                const uint64_t bd = smem_desc(st + n * spi * (kVKeys * 128) + kk * E::kKStep * 128,
+                                              kVKeys * 128, E::kVSbo, E::kVSwz);
+                mma_pair<T>(tmem + n * nn, ad, bd, idesc_pv, true);
+              }
+            }
+            mma_commit_pair_mc(smem_u32(&bars.empty[s]), pair_mask);
+            if (++s == kStages) { s = 0; phase ^= 1u; }
+            give_piece(kGroups);
+          }
           mma_commit_pair_mc(smem_u32(&bars.pv_done[gj & 1]), pair_mask);
           XATTN_TRACE_POINT(5, j);
         }
         if (!ok) break;
         mma_commit_pair_mc(smem_u32(&bars.o_done), pair_mask);
         g += w.n_tiles;
+        U = u_end;
       }
       mma_commit_pair_mc(smem_u32(&bars.drain), static_cast<uint16_t>(1u << rank));
       mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, nullptr);
@@ -462,10 +534,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t peer_x_empty0 = mapa_shared(smem_u32(&bars.x_empty[0]), dpeer);
     const uint32_t lead_s_free = mapa_shared(smem_u32(&bars.s_free), leader);
     const uint32_t lead_p_full0 = mapa_shared(smem_u32(&bars.p_full[0]), leader);
+    const uint32_t lead_o_lo_read = mapa_shared(smem_u32(&bars.o_lo_read), leader);
     const bool arm_thread = ((sw & 3) == 0 && lane == 0);  // one per group
 
     bool ok = true;
     int g = 0;   // global index of the item's first tile
+    int U = 0;   // piece use of the item's first piece
     int it = 0;  // items with tiles done
     // Exchange permissions.  My group sends piece use u = 2 g + grp into the D-peer's slot
     // u % 3.  Uses 0..2 find their slots free; use u >= 3 waits for the release of use u - 3
@@ -485,8 +559,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       const int gj = g + j;  // global tile index
       const int key0 = w.k_begin + j * kKeys;
       const int valid = min(kKeys, w.k_end - key0);
-      // my group's piece of tile gj: use u, slot u % 3, used for the (u / 3)-th time
-      const int u = 2 * gj + grp;
+      // my group's piece of tile gj: use u, slot u % 3, used for the (u / 3)-th time; the
+      // first tile of a folded range also exchanges the folded keys as use ux (8 per thread:
+      // keys 8 grp .. 8 grp + 7 of the fold, TMEM columns 0..15)
+      const bool fold = j == 0 && w.extra > 0;
+      const int u = U + 2 * j + (j > 0 && w.extra > 0 ? 1 : 0) + grp;
+      const int ux = U + kGroups;
       const int slot = u % kXSlots;
       const uint32_t x_par = static_cast<uint32_t>(u / kXSlots) & 1u;
       uint8_t* xcur = xbuf + slot * kPieceBytes;
@@ -496,13 +574,14 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       // fail at once through the abort flag), so every softmax warp reaches each named
       // barrier equally often and none is left in bar.sync.
       ok = ok && warp_mbar_wait(smem_u32(&bars.s_full), gj & 1, kTimeoutMmaDone, abort);
-      uint32_t ra[32], rb[32];
+      uint32_t ra[32], rb[32], rx[8];
       float gmax = -INFINITY;
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(6, j);
         tc_fence_after();
         tmem_ld32(t_row + kSCol + cbase, ra);
         tmem_ld32(t_row + kSCol + cbase + 32, rb);
+        if (fold) tmem_ld8(t_row + 8 * grp, rx);
         tmem_ld_wait();
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(18, j);
         tc_fence_before();
@@ -527,8 +606,22 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
                       __uint_as_float(rb[4 * i + 2]), __uint_as_float(rb[4 * i + 3]));
         if (arm_thread) mbar_arrive_expect_tx(smem_u32(&bars.x_full[slot]), kPieceBytes);
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(7, j);
-        ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[slot]), x_par, kTimeoutPeer, abort);
       }
+      if (fold && ok) {
+        const int sx = ux % kXSlots;
+        if (ux >= kXSlots)
+          ok = warp_mbar_wait<true>(smem_u32(&bars.x_empty[sx]), x_empty_parity(ux), kTimeoutExchange, abort);
+        if (ok) {
+          const uint32_t px = peer_x_row0 + sx * kPieceBytes;
+#pragma unroll
+          for (int k = 0; k < 2; ++k)
+            st_async_v4(px + (2 * grp + k) * (kRows * 16), peer_x_full0 + sx * 8, __uint_as_float(rx[4 * k]),
+                        __uint_as_float(rx[4 * k + 1]), __uint_as_float(rx[4 * k + 2]),
+                        __uint_as_float(rx[4 * k + 3]));
+          if (sw == 0 && lane == 0) mbar_arrive_expect_tx(smem_u32(&bars.x_full[sx]), kRows * kFold * 4);
+        }
+      }
+      if (ok) ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[slot]), x_par, kTimeoutPeer, abort);
       if (ok) {
         if (sw == 0 && lane == 0) XATTN_TRACE_POINT(8, j);
 #pragma unroll
@@ -542,6 +635,27 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
             gmax = fmaxf(gmax, t);
             rv = __float_as_uint(t);
+          }
+        }
+      }
+      if (fold && ok) {
+        const int sx = ux % kXSlots;
+        ok = warp_mbar_wait<true>(smem_u32(&bars.x_full[sx]), static_cast<uint32_t>(ux / kXSlots) & 1u,
+                                  kTimeoutPeer, abort);
+        if (ok) {
+          const uint8_t* xx = xbuf + sx * kPieceBytes;
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const float4 o = *reinterpret_cast<const float4*>(xx + x_offset(2 * grp + k, row));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
+              const float t = 8 * grp + 4 * k + e < w.extra
+                                  ? (__uint_as_float(rx[4 * k + e]) + add) * p.scale_log2
+                                  : -INFINITY;
+              gmax = fmaxf(gmax, t);
+              rx[4 * k + e] = __float_as_uint(t);
+            }
           }
         }
       }
@@ -613,13 +727,42 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
               make_uint4(h4[0], h4[1], h4[2], h4[3]);
         }
       }
+      if (fold) {
+        // the folded keys' P, K-major like the main P, 16 KB into the folded piece's slot
+        uint8_t* xx = xbuf + (ux % kXSlots) * kPieceBytes + 16384;
+        if constexpr (sizeof(T) == 4) {
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            uint32_t q4[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              q4[e] = f2tf32(ex2_approx(__uint_as_float(rx[4 * k + e]) - m_run));
+              lsum += __uint_as_float(q4[e]);
+            }
+            *reinterpret_cast<uint4*>(xx + p_offset(2 * grp + k, row)) = make_uint4(q4[0], q4[1], q4[2], q4[3]);
+          }
+        } else {
+          uint32_t h4[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __half2 hv = __floats2half2_rn(ex2_approx(__uint_as_float(rx[2 * e]) - m_run),
+                                                 ex2_approx(__uint_as_float(rx[2 * e + 1]) - m_run));
+            const float2 back = __half22float2(hv);
+            lsum += back.x + back.y;
+            h4[e] = *reinterpret_cast<const uint32_t*>(&hv);
+          }
+          *reinterpret_cast<uint4*>(xx + row * 128 + ((grp ^ (row & 7)) << 4)) =
+              make_uint4(h4[0], h4[1], h4[2], h4[3]);
+        }
+      }
       l_run += lsum;
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(16, j);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(17, j);
-      if (lane == 0) mbar_arrive_remote(lead_p_full0 + slot * 8);
+      if (lane == 0) mbar_arrive_remote(lead_p_full0 + slot * 8, kGroups);  // my group's piece
+      if (fold && lane == 0) mbar_arrive_remote(lead_p_full0 + (ux % kXSlots) * 8, 1u);
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(10, j);
     }
     // ---- epilogue of the item
@@ -655,9 +798,13 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       float* dst0 = p.split_mode
                         ? p.po + ((static_cast<size_t>(b) * p.n_latent + y0) * p.num_splits + split) * p.dim + col0
                         : p.out + (static_cast<size_t>(b) * p.n_latent + y0) * p.dim + col0;
-      const uint32_t stage = smem_u32(xbuf) + ((2 * (g + w.n_tiles) - 1) % kXSlots) * kPieceBytes;
+      const uint32_t stage = smem_u32(xbuf) + ((U + w.uses() - 1) % kXSlots) * kPieceBytes;
+      // a folded first tile of the next item writes TMEM columns 0..15: group 0's warps
+      // report when their first chunk (columns 0..31) has left TMEM
+      const int nxt = with_tiles(item + n_clusters);
+      const bool lo_wait = nxt < p.n_items && item_at(nxt).extra > 0;
       fused::store_o_direct(dst0, rs, stage + sw * 4096, t_row, dh, grp, lane, scale,
-                            min(32, p.n_latent - y0));
+                            min(32, p.n_latent - y0), lo_wait && grp == 0 ? lead_o_lo_read : 0u);
       tc_fence_before();
     } else if (w.n_tiles == 0 && p.split_mode && live) {
       const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
@@ -675,9 +822,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       if (with_tiles(item + n_clusters) < p.n_items) {
         named_bar_sync(1, kSoftmaxThreads);
         if (sw == 0 && lane == 0)
-          mbar_arrive_remote(peer_x_empty0 + ((2 * (g + w.n_tiles) - 1) % kXSlots) * 8);
+          mbar_arrive_remote(peer_x_empty0 + ((U + w.uses() - 1) % kXSlots) * 8);
       }
       g += w.n_tiles;
+      U += w.uses();
       ++it;
     }
     }

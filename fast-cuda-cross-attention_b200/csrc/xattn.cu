@@ -266,6 +266,7 @@ int launch_fused_pair(const T* Q, const T* K, const T* V, float* out, float* po,
     const uint64_t sk[2] = {(uint64_t)D * es, (uint64_t)Ni * D * es};
     const uint32_t bq[3] = {(uint32_t)E::kCols, fused::kRows, 1};
     const uint32_t bk[3] = {(uint32_t)E::kCols, fused::kKeys / 2, 1};
+    const uint32_t bk8[3] = {(uint32_t)E::kCols, pair4::kFold / 2, 1};  // folded keys, half per CTA
     // V as [B][D/kCols slabs][Ni keys][kCols columns]: one box holds all the slabs a CTA
     // needs for one P.V instruction (dh / n_instr / 2 columns), so a V stage is one copy
     // per instruction
@@ -275,6 +276,7 @@ int launch_fused_pair(const T* Q, const T* K, const T* V, float* out, float* po,
     const uint32_t bv[4] = {(uint32_t)E::kCols, (uint32_t)E::kVKeys, (uint32_t)spi, 1};
     if (!encode_tmap(&p.tq, dt, 3, Q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_tmap(&p.tk, dt, 3, K, dk, sk, bk, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !encode_tmap(&p.tk8, dt, 3, K, dk, sk, bk8, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !encode_tmap(&p.tv, dt, 4, V, dv, sv, bv,
                      sizeof(T) == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B))
       return XATTN_ERR_ARG;

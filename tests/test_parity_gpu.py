@@ -151,6 +151,9 @@ PAIR_SHAPES = [
     # more 256-row items than co-resident clusters (33 on a B200): the persistent clusters
     # loop over items with one, two and several key tiles each
     (40, 256, 100, 768), (36, 512, 200, 768), (70, 256, 300, 256), (40, 256, 784, 768),
+    # key ranges whose last 1..16 keys fold into the first tile (N_input % 128 in 1..16):
+    # one tile plus the fold, persistent with folds, several tiles plus the fold
+    (8, 256, 136, 768), (34, 256, 136, 512), (36, 512, 400, 768), (2, 256, 257, 256),
 ]
 
 
