@@ -17,29 +17,35 @@
 // Persistent: one cluster per co-resident slot loops over the items (batch, 256-row block,
 // key split); the ring, the MMA issuer's ring position and every per-tile barrier phase
 // continue across items on a global tile index, so the next item's operands stream while
-// the current item finishes.  The epilogue stages O (32 x 32 boxes) in the exchange buffers
-// and writes it with TMA stores.
+// the current item finishes.  The epilogue takes O out of TMEM in 32 x 32 chunks, passes each
+// through a 4 KB shared-memory box per warp (in the slot of the item's last exchange piece)
+// and writes whole 128-byte row segments with 16-byte stores (fused::store_o_direct).
 //
 // Pair protocol.  TMA loads of both CTAs complete on the leader's full barrier; the
 // leader's commits are multicast to both CTAs (empty, s_full, pv_done, o_done) or to the
-// D-peer pair (x_empty); the
-// softmax warps of both CTAs release S and publish P by one arrival per warp on the
-// leader's s_free / p_full barriers.  No TMA multicast is used.
+// D-peer pair (x_empty); the softmax warps of both CTAs release S and publish P by arrivals
+// on the leader's s_free / p_full barriers.  No TMA multicast is used.
 //
 // Operand ring.  Three producer warps share one ring of five 24 KB stages in the order
 // QK(0), then per tile QK(j+1), V(j): a Q/K stage is a 128-byte-wide chunk of the CTA's 128
 // Q rows and of its half of the K tile, a V stage one 4-D box of keys x the CTA's V slabs.
 // Producer 0 also prefetches into L2 the V of the tile being loaded and each producer the
-// next tile's K chunk it will load, so fewer stage round trips wait on DRAM.  The stream of
-// stages through this ring, not the softmax, sets the pace of the fp32 kernel: its depth is
-// bounded by the exchange / P slots beside it.
+// next tile's K chunk it will load, so fewer stage round trips wait on DRAM.  With five
+// stages the stream keeps up: timing builds that skip every load after an item's first
+// tile run within 1-2 % of this kernel, whose pace is the tensor-core instruction stream
+// and the item boundaries (epilogue, then the next item's first exchange).
 //
 // Exchange slots.  The partial scores travel in pieces of half a key tile (one softmax
 // group's 64 keys): piece use u = 2 g + group of global tile g lands in slot u % 3 of the
 // D-peer, where the peer's softmax then writes P over it.  The pair leader hands a slot back
 // to the D-peer pair with a commit multicast to both of its CTAs once the P.V instructions
 // that read the piece complete (an arrival on their x_empty barrier, no data), so the next
-// tile's second piece waits only for the first half of this tile's P.V.
+// tile's second piece waits only for the first half of this tile's P.V.  An item's last
+// piece is handed back after its epilogue instead, which stages O in that slot.
+//
+// Folded remainder.  A key range whose last 1..kFold keys would form a short last tile adds
+// them to its first tile: an N = 16 Q.K^T per stage into TMEM columns 0..15 (O's, unused
+// until that tile's P.V), an extra exchange piece and an extra V stage (see kFold).
 #pragma once
 
 #include <cuda_fp16.h>
