@@ -1038,7 +1038,11 @@ extern "C" int xattn_splitk_noalloc(const float* Q, const float* K, const float*
   if (output == nullptr) return set_error(XATTN_ERR_ARG);
   if (N_input == 0) return set_error(zero_output(output, batch_size, N_latent, dim, stream));
   if (Q == nullptr || K == nullptr || V == nullptr) return set_error(XATTN_ERR_ARG);
-  const size_t rows = static_cast<size_t>(batch_size) * N_latent;
+  const size_t rows = static_cast<size_t>(batch_size) * N_latent;  // >= 1, < 2^62
+  // rows * num_splits * (dim + 2) <= capacity, tested by division so that no product can
+  // wrap around (each factor is below 2^62 and 2^32)
+  const size_t per_row = static_cast<size_t>(num_splits) * (static_cast<size_t>(dim) + 2);
+  if (per_row > kNoAllocScratchFloats / rows) return set_error(XATTN_ERR_TOO_LARGE);
   const size_t po_elems = round_up64(rows * num_splits * dim);
   const size_t ml_elems = round_up64(rows * num_splits);
   if (po_elems + 2 * ml_elems > kNoAllocScratchFloats) return set_error(XATTN_ERR_TOO_LARGE);

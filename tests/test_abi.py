@@ -66,6 +66,25 @@ def test_library_loads_without_gpu_and_reports_version():
     assert lib.xattn_last_error() == 0
 
 
+def test_noalloc_size_limit_cannot_wrap_around():
+    """xattn_splitk_noalloc refuses oversize problems before any CUDA call or pointer use.
+
+    With B = N_latent = 2^17 and num_splits = 2^30, B * N_latent * num_splits is 2^64, which
+    a plain size_t product wraps to zero (and with it every scratch size derived from it);
+    the entry must still answer XATTN_ERR_TOO_LARGE (5).  The pointers are never
+    dereferenced: the size check precedes every device operation.
+    """
+    lib = ctypes.CDLL(LIB)
+    fn = lib.xattn_splitk_noalloc
+    fn.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 5 + [ctypes.c_void_p]
+    fn.restype = ctypes.c_int
+    fake = 256  # non-null, 16-byte aligned, never read
+    assert fn(fake, fake, fake, fake, 1 << 17, 1 << 17, 784, 768, 1 << 30, None) == 5
+    assert fn(fake, fake, fake, fake, 4, 1024, 784, 768, 8, None) == 5  # just over 32 MiB
+    lib.xattn_last_error.restype = ctypes.c_int
+    assert lib.xattn_last_error() == 5
+
+
 def test_cudart_is_linked_shared():
     out = subprocess.run(["ldd", LIB], capture_output=True, text=True).stdout
     assert "libcudart.so" in out
