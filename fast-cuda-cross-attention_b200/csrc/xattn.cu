@@ -21,6 +21,7 @@
 #include <map>
 #include <mutex>
 #include <tuple>
+#include <vector>
 #include <utility>
 
 #include "accurate.cuh"
@@ -124,28 +125,53 @@ int sm_count(int dev) { return g_dev[dev].sms > 0 ? g_dev[dev].sms : 148; }
 
 // Library workspace for automatic key splits: one grow-only buffer per (device, stream).
 // Calls that share a stream are ordered by it; different streams get different buffers.
+//
+// CUDA graphs: a call captured into a graph bakes the stream's buffer address into it, so a
+// buffer that captured work used is never freed (a later growth retires it, and retired
+// buffers live until the process exits).  A capture on a stream without a large enough
+// buffer allocates one with the thread's capture mode relaxed for that cudaMalloc (an
+// allocation enqueues no work on the captured stream).  Graph replays share the buffer
+// with calls on the stream they were captured on: order them.
 struct Workspace {
   void* ptr = nullptr;
   size_t bytes = 0;
+  bool captured = false;  // handed to work that a stream capture recorded
 };
 std::map<std::pair<int, cudaStream_t>, Workspace> g_ws;
+std::vector<void*> g_ws_retired;  // outgrown buffers that captured graphs may still read
 
 void* workspace(int dev, cudaStream_t stream, size_t bytes) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  Workspace& w = g_ws[{dev, stream}];
-  if (w.bytes >= bytes) return w.ptr;
-  if (w.ptr != nullptr) {
-    cudaStreamSynchronize(stream);
-    cudaFree(w.ptr);
-    w.ptr = nullptr;
-    w.bytes = 0;
-  }
-  size_t grow = std::max(bytes, static_cast<size_t>(16) << 20);
-  if (cudaMalloc(&w.ptr, grow) != cudaSuccess) {
-    w.ptr = nullptr;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess) {
+    cudaGetLastError();  // e.g. the legacy stream while another thread captures
     return nullptr;
   }
-  w.bytes = grow;
+  const bool capturing = cap != cudaStreamCaptureStatusNone;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace& w = g_ws[{dev, stream}];
+  if (w.bytes < bytes) {
+    if (w.ptr != nullptr) {
+      if (capturing || w.captured) {
+        g_ws_retired.push_back(w.ptr);  // no synchronisation is possible (or safe) here
+      } else {
+        cudaStreamSynchronize(stream);
+        cudaFree(w.ptr);
+      }
+      w = Workspace{};
+    }
+    const size_t grow = std::max(bytes, static_cast<size_t>(16) << 20);
+    cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+    if (capturing) cudaThreadExchangeStreamCaptureMode(&mode);
+    const cudaError_t rc = cudaMalloc(&w.ptr, grow);
+    if (capturing) cudaThreadExchangeStreamCaptureMode(&mode);  // back to the caller's mode
+    if (rc != cudaSuccess) {
+      cudaGetLastError();
+      w = Workspace{};
+      return nullptr;
+    }
+    w.bytes = grow;
+  }
+  if (capturing) w.captured = true;
   return w.ptr;
 }
 

@@ -49,7 +49,12 @@ void launch_tiled_kernel(const float* Q, const float* K, const float* V, float* 
 /* Replaces launch_optimized_kernel (kernel_vectorized.cu:198-215; cuda_wrappers.py:122-133).
  * fp32 in/out, tcgen05 kind::tf32 tensor cores with fp32 accumulation; picks a key split
  * on its own when batch_size * N_latent is too small to fill the GPU (library-owned
- * workspace, allocated once per device and stream and grown on demand).                */
+ * workspace, allocated once per device and stream and grown on demand).
+ * CUDA graphs: after one call on the device outside any capture (its one-time set-up),
+ * calls can be captured on any stream; a workspace that captured work used is never
+ * freed (it is retired, not freed, when the stream's workspace grows), so a graph stays
+ * valid after later, larger calls.  Replays share that workspace with calls on the
+ * stream the graph was captured on: order them on one stream.                          */
 void launch_optimized_kernel(const float* Q, const float* K, const float* V, float* output,
                              int batch_size, int N_latent, int N_input, int dim,
                              cudaStream_t stream);
