@@ -189,6 +189,9 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
+  // a split's combine kernel, launched as a programmatic dependent, may take free SM slots
+  // now and wait there for this grid's results
+  griddep_launch_dependents();
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();

@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
                                                                   float* __restrict__ pm_out = nullptr,
                                                                   float* __restrict__ pl_out = nullptr) {
   extern __shared__ float w[];
+  griddep_wait();  // launched as a programmatic dependent of the kernel writing the partials
   const long long r = blockIdx.x;
   if (r >= rows) return;
   const float* m = pm + r * num_splits;

@@ -540,6 +540,16 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Programmatic dependent launch.  launch_dependents lets the next kernel of the stream,
+// when it was launched with programmatic stream serialization, start its CTAs once every
+// CTA of this grid has executed it (or exited); that kernel's griddep_wait() then blocks
+// until this grid has completed and its memory operations are visible.  Both are no-ops
+// for launches without the attribute.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ bool elect_one() {
   uint32_t pred = 0;
   asm volatile(

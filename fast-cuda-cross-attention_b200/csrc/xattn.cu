@@ -417,10 +417,23 @@ int launch_combine(const float* po, const float* pm, const float* pl, float* out
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            static_cast<int>(smem)) != cudaSuccess)
     return XATTN_ERR_LAUNCH;
-  const dim3 grid(static_cast<unsigned>(rows), (D + simt::kCombineCols - 1) / simt::kCombineCols);
-  kern<<<grid, simt::kCombineThreads, smem, stream>>>(po, pm, pl, out, rows, D, num_splits, D, pm_out,
-                                                      pl_out);
-  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+  // Programmatic stream serialization: the combine's CTAs may launch while the partial
+  // kernel still runs (the pair kernel triggers at its start) and wait in griddep_wait()
+  // for its results, so the kernel boundary costs no launch latency.  After any other
+  // stream operation this is ordinary stream order.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(rows), (D + simt::kCombineCols - 1) / simt::kCombineCols);
+  cfg.blockDim = dim3(simt::kCombineThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t rc = cudaLaunchKernelEx(&cfg, kern, po, pm, pl, out, rows, D, num_splits, D,
+                                            pm_out, pl_out);
+  return rc == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 
 bool bad_sizes(int B, int Nl, int Ni, int D) { return B < 0 || Nl < 0 || Ni < 0 || D <= 0; }
