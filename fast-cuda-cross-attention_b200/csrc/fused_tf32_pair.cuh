@@ -278,6 +278,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   volatile int* abort = &abort_flag;
+  // Launched as a programmatic dependent: the set-up above (barriers, tensor memory, tensor
+  // map prefetch) touches no global memory and overlaps the previous kernel of the stream;
+  // nothing below reads inputs or writes outputs before that kernel has completed.
+  griddep_wait();
 
   if (warp == 0 || warp >= kFirstExtraProducer) {
     // ================================================================ TMA producers (both CTAs)

@@ -330,9 +330,20 @@ int launch_fused_pair(const T* Q, const T* K, const T* V, float* out, float* po,
   cudaGetDevice(&dev);
   const int slots = dev >= 0 && dev < 64 ? g_dev[dev].pair_slots : 0;
   const long long clusters = slots > 0 ? std::min<long long>(items, slots) : items;
-  pair4::fused_tf32_pair_kernel<T><<<static_cast<unsigned>(clusters * 4), pair4::kThreads,
-                                     pair4::kSmemBytes, stream>>>(p);
-  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+  // programmatic stream serialization: the kernel's set-up overlaps the previous kernel of
+  // the stream, and it waits (griddepcontrol.wait) before touching global memory
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(clusters * 4));
+  cfg.blockDim = dim3(pair4::kThreads);
+  cfg.dynamicSmemBytes = pair4::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, pair4::fused_tf32_pair_kernel<T>, p) == cudaSuccess ? XATTN_OK
+                                                                                  : XATTN_ERR_LAUNCH;
 }
 
 int launch_fused_pair(const float* Q, const float* K, const float* V, float* out, int B, int Nl,
