@@ -30,12 +30,14 @@
 //
 // TF32 truncation bias.  kind::tf32 drops the low 13 mantissa bits of each fp32 operand
 // (truncation, measured on B200), which shrinks every operand by its relative truncation
-// error e.  For mantissas spread log-uniformly over an octave (Gaussian data, most real
-// data) E[e] = 2^-11 * E[1/m] = 2^-11 / (2 ln 2) = 3.522e-4, so Q.K^T comes out scaled by
-// ~(1 - 2E[e]) -- a softmax temperature shift that dominates the error -- and P.V by
-// ~(1 - E[e]).  By default the host multiplies the score scale by (1 + 2E[e]) and the
-// output by (1 + E[e]) (out_comp), which removes the systematic part; the option can be
-// switched off for inputs that are already exactly representable in TF32.
+// error.  Q.K^T comes out scaled by ~(1 - e_Q - e_K) -- a softmax temperature shift that
+// dominates the error -- and P.V by ~(1 - e_V), where e_X is the least-squares relative
+// truncation of operand X: e = sum(d x) / sum(x x) with d = x - trunc_tf32(x).  By default
+// every item measures e_Q (its own query rows), e_K and e_V (its key range) on a sample of
+// the inputs (trunc_load / trunc_finish) and scales the scores by (1 + e_Q + e_K) and the
+// output by (1 + e_V).  Random fp32 mantissas give e ~ 2^-11 / (2 ln 2) = 3.5e-4 each;
+// inputs that are already exact in TF32 (widened bf16 / fp16, small integers) give exactly
+// e = 0, so they are computed without any compensation.
 //
 // Warp roles (64 + 128 * kGroups threads): warp 0 = TMA producer, warp 1 = MMA issuer,
 // warps 2.. = softmax / exchange / epilogue.  Softmax warp w reads TMEM lanes
@@ -100,9 +102,145 @@ struct Params {
   int split_chunk;   // keys per split (upstream rule: ceil(Ni / S))
   int split_mode;    // 0: normalised output, 1: partial triples
   int n_items;       // work items (persistent kernels loop over them)
-  float scale_log2;  // log2(e) / sqrt(D), times the score bias compensation
-  float out_comp;    // output bias compensation (1 when off)
+  float scale_log2;  // log2(e) / sqrt(D) (times a fixed score compensation in comp_mode 2)
+  float out_comp;    // fixed output compensation (1 unless comp_mode 2)
+  int comp_mode;     // 1: measure the truncation of the inputs per item (fp32 operands only)
+  const float* q;    // the inputs as plain pointers, read by the truncation sampling
+  const float* k;
+  const float* v;
 };
+
+// ------------------------------------------------------------------ truncation compensation
+// Sample of one item's inputs, loaded by one softmax thread t in [0, 256): a 16-byte piece
+// of its own query row, one of K and one of V at positions spread over the item's key range
+// (1024 values of each per CTA).  Positions depend on the item, the row and t only, never on
+// the CTA's half of D, so the CTAs that share rows (and exchange scores) measure
+// bit-identical factors.
+constexpr int kTruncPieces = 1;
+struct TruncLoads {
+  float4 q[kTruncPieces], k[kTruncPieces], v[kTruncPieces];
+};
+
+__device__ __forceinline__ void trunc_load(const Params& p, TruncLoads& s, int b, int qrow, int k_begin,
+                                           int k_end, int t) {
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int c4 = p.dim / 4;  // 16-byte pieces per row (D % 64 == 0 on this path)
+  const int nk = k_end - k_begin;
+#pragma unroll
+  for (int i = 0; i < kTruncPieces; ++i) {
+    const int cq = 4 * static_cast<int>((static_cast<unsigned>(qrow) * 13u + (2u * t + i) * 97u + 5u) % c4);
+    s.q[i] = qrow < p.n_latent
+                 ? __ldg(reinterpret_cast<const float4*>(p.q + (static_cast<size_t>(b) * p.n_latent + qrow) * p.dim + cq))
+                 : zero;
+    const int key = k_begin + static_cast<int>((static_cast<long long>(2 * t + i) * nk) >> 9);
+    const size_t kr = (static_cast<size_t>(b) * p.n_input + key) * p.dim;
+    const int ck = 4 * static_cast<int>((static_cast<unsigned>(t) * 29u + i * 131u + 3u) % c4);
+    const int cv = 4 * static_cast<int>((static_cast<unsigned>(t) * 53u + i * 71u + 17u) % c4);
+    s.k[i] = nk > 0 ? __ldg(reinterpret_cast<const float4*>(p.k + kr + ck)) : zero;
+    s.v[i] = nk > 0 ? __ldg(reinterpret_cast<const float4*>(p.v + kr + cv)) : zero;
+  }
+}
+
+// sum(d x) and sum(x x) of the four values, d = x - trunc_tf32(x)
+__device__ __forceinline__ void trunc_add(const float4& x, float& num, float& den) {
+  const float e[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float t = __uint_as_float(__float_as_uint(e[i]) & 0xFFFFE000u);
+    num = fmaf(e[i] - t, e[i], num);
+    den = fmaf(e[i], e[i], den);
+  }
+}
+
+// Relative truncation from the sums; 0 when nothing was sampled, and for non-finite sums
+// (NaN / Inf inputs, overflowing squares), where no compensation is the safe answer.
+__device__ __forceinline__ float trunc_ratio(float num, float den) {
+  return fminf(fmaxf(num / den, 0.f), 0.0009765625f);  // fmaxf(NaN, 0) = 0; |d| < 2^-10 |x|
+}
+
+// Truncation sums of one item of the four-CTA pair kernel, taken by one warp: one 16-byte
+// piece of each of the item's 256 query rows (rows past N_latent skipped), kept apart per
+// 128-row half, and 128 pieces each of K and V spread over the key range [k_begin, k_end)
+// -- 512 values of each.  s = {sum d x, sum x x} of rows 0..127, of rows 128..255, of K, of
+// V, identical in every lane (xor butterfly).  All sixteen loads are issued before any is
+// used (one memory round trip).  Positions depend on the item only, so the two pairs of a
+// cluster (the two halves of D) compute bit-identical sums.
+__device__ __forceinline__ int trunc_piece_col(unsigned key, unsigned c4) {
+  return 4 * static_cast<int>(__umulhi(key * 0x9E3779B1u, c4));  // hashed 16-byte piece < c4
+}
+__device__ __forceinline__ void trunc_warp_sample(const Params& p, int b, int row_base, int k_begin,
+                                                  int k_end, int lane, float (&s)[8]) {
+  const unsigned c4 = static_cast<unsigned>(p.dim / 4);  // 16-byte pieces per row
+  const int nk = k_end - k_begin;
+  const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 x[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // query rows row_base + lane + 32 i
+    const int row = row_base + lane + 32 * i;
+    x[i] = row < p.n_latent
+               ? __ldg(reinterpret_cast<const float4*>(p.q + (static_cast<size_t>(b) * p.n_latent + row) * p.dim +
+                                                       trunc_piece_col(static_cast<unsigned>(row), c4)))
+               : zero;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // K (i < 4) and V pieces 0..127
+    const unsigned piece = static_cast<unsigned>(lane + 32 * (i & 3));
+    const int key = k_begin + static_cast<int>((static_cast<long long>(piece) * nk) >> 7);
+    const float* src = i < 4 ? p.k : p.v;
+    x[8 + i] = nk > 0 ? __ldg(reinterpret_cast<const float4*>(src + (static_cast<size_t>(b) * p.n_input + key) * p.dim +
+                                                              trunc_piece_col(piece * 2u + (i < 4 ? 1u : 2u), c4)))
+                      : zero;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s[i] = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int t = i < 4 ? 0 : (i < 8 ? 1 : (i < 12 ? 2 : 3));  // rows 0..127, 128..255, K, V
+    trunc_add(x[i], s[2 * t], s[2 * t + 1]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i] += __shfl_xor_sync(0xffffffffu, s[i], o);
+}
+
+// This thread's sums of its sample: {sum d x, sum x x} for Q, K and V.
+__device__ __forceinline__ void trunc_fold(const TruncLoads& s, float (&v)[6]) {
+#pragma unroll
+  for (int i = 0; i < 6; ++i) v[i] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kTruncPieces; ++i) {
+    trunc_add(s.q[i], v[0], v[1]);
+    trunc_add(s.k[i], v[2], v[3]);
+    trunc_add(s.v[i], v[4], v[5]);
+  }
+}
+
+// Warp sums of the threads' sums into buf[sw] (a [kWarps][6] array in shared memory).
+__device__ __forceinline__ void trunc_publish(float (&v)[6], float (*buf)[6], int sw, int lane) {
+  // xor butterfly: every lane ends with bit-identical sums
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int i = 0; i < 6; ++i) v[i] += __shfl_xor_sync(0xffffffffu, v[i], o);
+  if (lane == 0)
+#pragma unroll
+    for (int i = 0; i < 6; ++i) buf[sw][i] = v[i];
+}
+
+// Once every softmax warp published into `buf` and a barrier ordered that: the score factor
+// (1 + e_Q + e_K) and the output factor (1 + e_V), identical in every thread (same sums,
+// same order).  No warp may publish into `buf` again before every thread has read it.
+template <int kWarps>
+__device__ __forceinline__ void trunc_ratios(const float (*buf)[6], float& score_factor,
+                                             float& out_factor) {
+  float t[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int w = 0; w < kWarps; ++w)
+#pragma unroll
+    for (int i = 0; i < 6; ++i) t[i] += buf[w][i];
+  score_factor = 1.f + trunc_ratio(t[0], t[1]) + trunc_ratio(t[2], t[3]);
+  out_factor = 1.f + trunc_ratio(t[4], t[5]);
+}
 
 struct __align__(8) Barriers {
   uint64_t full[kStages];
@@ -267,6 +405,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* xbuf = smem + kStages * kStageBytes;
   __shared__ Barriers bars;
   __shared__ float red[kGroups][kRows];  // per-group row maxima, then row sums (epilogue)
+  __shared__ float tstat[kSoftmaxThreads / 32][6];  // truncation sums per softmax warp
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -470,6 +609,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     float m_true = -INFINITY;  // exact running max (log2 units)
     float l_run = 0.f;         // this group's share of the row sum
     bool ok = true;
+    // Score scale and output factor, with the measured truncation compensation: the sample
+    // is loaded and published now (its loads overlap the first Q.K^T) and reduced after the
+    // first tile's named barrier; scores are scaled only after it (the row maximum is taken
+    // on unscaled sums, which scaling by a positive factor keeps in order).
+    const bool comp = p.comp_mode == 1 && n_tiles > 0;
+    float sl2 = p.scale_log2, oc = p.out_comp;
+    if (comp) {
+      TruncLoads tl;
+      trunc_load(p, tl, b, row0 + row, k_begin, k_end, sw * 32 + lane);
+      float sums[6];
+      trunc_fold(tl, sums);
+      trunc_publish(sums, tstat, sw, lane);
+    }
     for (int j = 0; j < n_tiles; ++j) {
       const int key0 = k_begin + j * kKeys;
       const int valid = min(kKeys, k_end - key0);
@@ -523,7 +675,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const int key = cbase + 4 * i + e;
           uint32_t& rv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
           const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
-          const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
+          const float t = key < valid ? __uint_as_float(rv) + add : -INFINITY;  // unscaled
           gmax = fmaxf(gmax, t);
           rv = __float_as_uint(t);
         }
@@ -540,6 +692,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       // the row maxima are read by both groups before either writes the next tile's
       named_bar_sync(2 + quad, 32 * kGroups);
       if (!ok) continue;
+      if (comp && j == 0) {  // every warp published its sample before the barrier above
+        float fs, fo;
+        trunc_ratios<kSoftmaxThreads / 32>(tstat, fs, fo);
+        sl2 *= fs;
+        oc *= fo;
+      }
+      tmax *= sl2;  // log2 units from here on
       m_true = fmaxf(m_true, tmax);
       float alpha = 1.f;
       if (j == 0) {
@@ -573,7 +732,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const uint32_t tv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
-          q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
+          q4[e] = f2tf32(ex2_approx(fmaf(__uint_as_float(tv), sl2, -m_run)));
           lsum += __uint_as_float(q4[e]);
         }
         *reinterpret_cast<uint4*>(xcur + p_offset(ch0 + i, row)) =
@@ -609,14 +768,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (p.split_mode) {
         // Partials relative to the exact max: O' = O * 2^(m_run - m_true), l' likewise.
         const float f = ex2_approx(m_run - m_true);
-        scale = f * p.out_comp;
+        scale = f * oc;
         const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
         if (live && h == 0 && grp == 0) {
           p.pm[pidx] = m_true * 0.69314718055994531f;
           p.pl[pidx] = l_tot * f;
         }
       } else {
-        scale = p.out_comp / l_tot;
+        scale = oc / l_tot;
       }
       // every MMA has completed, so the ring and the exchange buffers (the first 224 KB of
       // dynamic shared memory) are free: 24 KB of staging per softmax warp

@@ -171,6 +171,8 @@ struct __align__(8) Barriers {
   uint64_t o_lo_read;        // leader: both CTAs' epilogues read O's first 32 columns (a
                              // folded Q.K^T of the next item writes columns 0..15)
   uint64_t drain;            // leader: its MMAs completed
+  uint64_t stats_full[2];    // both: the truncation factors of item k are in tfac[k % 2]
+  uint64_t stats_empty[2];   // non-leader: the pair's softmax warps are done with tfac[k % 2]
 };
 
 template <typename T>
@@ -186,6 +188,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   uint8_t* kxbuf = xbuf + kXRegion;  // folded K rows, one kKxBytes box per ring slot
   __shared__ Barriers bars;
   __shared__ float red[kGroups][kRows];
+  __shared__ __align__(8) float tfac[2][2];  // per item parity: score factor of this CTA's rows, output factor
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
 
@@ -201,6 +204,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t dpeer = rank ^ 2u;       // same rows, other D half
   const uint16_t pair_mask = static_cast<uint16_t>(3u << leader);
   const bool is_leader = (r == 0);
+  // measured TF32 truncation compensation (fp32 operands; fused_tf32.cuh)
+  const bool comp = sizeof(T) == 4 && p.comp_mode == 1;
 
   // ---- work items: (batch, 256-row block, split); the cluster takes items cid,
   // cid + n_clusters, ...  Every role walks the same sequence and numbers the key tiles of
@@ -261,6 +266,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     mbar_init(smem_u32(&bars.o_done), 1);
     mbar_init(smem_u32(&bars.o_lo_read), kSoftmaxWarpsPerPair / kGroups);
     mbar_init(smem_u32(&bars.drain), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(smem_u32(&bars.stats_full[i]), 1);
+      mbar_init(smem_u32(&bars.stats_empty[i]), kSoftmaxWarpsPerPair);
+    }
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -532,6 +541,39 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       }
       mma_commit_pair_mc(smem_u32(&bars.drain), static_cast<uint16_t>(1u << rank));
       mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, nullptr);
+    } else if (!is_leader && comp) {
+      // ============================================================ truncation statistics
+      // Warp 1 of the pair's second CTA issues nothing, so it measures the inputs' TF32
+      // truncation for the items ahead of the softmax warps: per item, the score factor of
+      // each 128-row half, 1 + e_Q(half) + e_K, and the output factor 1 + e_V, written to
+      // tfac[k % 2] of the leader (first half) and of this CTA (second half) with st.async,
+      // whose bytes complete stats_full[k % 2] there (no fence needed).  Buffer k % 2 is
+      // refilled once the pair's sixteen softmax warps are done with item k - 2.
+      const uint32_t lead_fac = mapa_shared(smem_u32(&tfac[0][0]), leader);
+      const uint32_t own_fac = mapa_shared(smem_u32(&tfac[0][0]), rank);
+      const uint32_t lead_full = mapa_shared(smem_u32(&bars.stats_full[0]), leader);
+      const uint32_t own_full = mapa_shared(smem_u32(&bars.stats_full[0]), rank);
+      bool ok = true;
+      int k = 0;
+      for (int item = with_tiles(cid); item < p.n_items && ok; item = with_tiles(item + n_clusters), ++k) {
+        const int buf = k & 1;
+        if (k >= 2 &&
+            !(ok = warp_mbar_wait(smem_u32(&bars.stats_empty[buf]), static_cast<uint32_t>((k >> 1) - 1) & 1u,
+                                  kTimeoutSoftmax, abort)))
+          break;
+        const Item f = item_at(item);  // f.row0: this CTA's (second) row half
+        float sums[8];
+        fused::trunc_warp_sample(p, f.b, f.row0 - kRows, f.k_begin, f.k_end, lane, sums);
+        const float ek = fused::trunc_ratio(sums[4], sums[5]);
+        const float fo = 1.f + fused::trunc_ratio(sums[6], sums[7]);
+        if (lane == 0) {
+          st_async_v2(lead_fac + buf * 8, lead_full + buf * 8, 1.f + fused::trunc_ratio(sums[0], sums[1]) + ek, fo);
+          st_async_v2(own_fac + buf * 8, own_full + buf * 8, 1.f + fused::trunc_ratio(sums[2], sums[3]) + ek, fo);
+          mbar_arrive_expect_tx_cluster(lead_full + buf * 8, 8);
+          mbar_arrive_expect_tx_cluster(own_full + buf * 8, 8);
+        }
+        __syncwarp();
+      }
     }
   } else {
     // ================================================================ softmax / epilogue (both)
@@ -562,12 +604,20 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     // the output in that piece's slot (the next item's first pieces go to the other two
     // slots, so they cross while the epilogue runs).
     auto x_empty_parity = [&](int u) -> uint32_t { return static_cast<uint32_t>(u / kXSlots - 1) & 1u; };
+    // Truncation compensation: the statistics warp has an item's factors ready in
+    // tfac[it % 2] long before its first tile needs them; every softmax thread acquires them
+    // while the previous item's epilogue waits for its last P.V (the first item's at its
+    // first tile).  Scores are scaled only after the first tile's row-maximum barrier (the
+    // maximum is taken on unscaled sums, whose order a positive factor keeps), by one FFMA
+    // inside the exponent.
+    const uint32_t stats_empty0 = mapa_shared(smem_u32(&bars.stats_empty[0]), leader | 1u);
     for (int item = cid; item < p.n_items; item += n_clusters) {
       const Item w = item_at(item);
       const int b = w.b, split = w.split, row0 = w.row0;
       float m_run = -INFINITY;
       float m_true = -INFINITY;
       float l_run = 0.f;
+      float sl2 = p.scale_log2;  // this item's score scale (compensated at its first tile)
     for (int j = 0; j < w.n_tiles; ++j) {
       const int gj = g + j;  // global tile index
       const int key0 = w.k_begin + j * kKeys;
@@ -645,7 +695,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             const int key = cbase + 4 * i + e;
             uint32_t& rv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
             const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
-            const float t = key < valid ? (__uint_as_float(rv) + add) * p.scale_log2 : -INFINITY;
+            const float t = key < valid ? __uint_as_float(rv) + add : -INFINITY;  // unscaled
             gmax = fmaxf(gmax, t);
             rv = __float_as_uint(t);
           }
@@ -664,7 +714,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 4; ++e) {
               const float add = e == 0 ? o.x : (e == 1 ? o.y : (e == 2 ? o.z : o.w));
               const float t = 8 * grp + 4 * k + e < w.extra
-                                  ? (__uint_as_float(rx[4 * k + e]) + add) * p.scale_log2
+                                  ? __uint_as_float(rx[4 * k + e]) + add
                                   : -INFINITY;
               gmax = fmaxf(gmax, t);
               rx[4 * k + e] = __float_as_uint(t);
@@ -681,6 +731,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
       named_bar_sync(2 + quad, 32 * kGroups);
       if (!ok) continue;
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(15, j);
+      if (comp && j == 0) {
+        if (it == 0 && !(ok = warp_mbar_wait<true>(smem_u32(&bars.stats_full[0]), 0u, kTimeoutSoftmax, abort)))
+          continue;
+        sl2 = p.scale_log2 * tfac[it & 1][0];
+      }
+      tmax *= sl2;  // log2 units from here on
       m_true = fmaxf(m_true, tmax);
       float alpha = 1.f;
       if (j == 0) {
@@ -714,7 +770,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const uint32_t tv = i < 8 ? ra[4 * i + e] : rb[4 * (i - 8) + e];
-            q4[e] = f2tf32(ex2_approx(__uint_as_float(tv) - m_run));
+            q4[e] = f2tf32(ex2_approx(fmaf(__uint_as_float(tv), sl2, -m_run)));
             lsum += __uint_as_float(q4[e]);
           }
           *reinterpret_cast<uint4*>(xcur + p_offset(i, row)) =
@@ -730,8 +786,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 4; ++e) {
             const int k = 8 * c + 2 * e;
             const uint32_t t0 = k < 32 ? ra[k] : rb[k - 32], t1 = k + 1 < 32 ? ra[k + 1] : rb[k + 1 - 32];
-            const __half2 hv = __floats2half2_rn(ex2_approx(__uint_as_float(t0) - m_run),
-                                                 ex2_approx(__uint_as_float(t1) - m_run));
+            const __half2 hv = __floats2half2_rn(ex2_approx(fmaf(__uint_as_float(t0), sl2, -m_run)),
+                                                 ex2_approx(fmaf(__uint_as_float(t1), sl2, -m_run)));
             const float2 back = __half22float2(hv);
             lsum += back.x + back.y;
             h4[e] = *reinterpret_cast<const uint32_t*>(&hv);
@@ -749,7 +805,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t q4[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-              q4[e] = f2tf32(ex2_approx(__uint_as_float(rx[4 * k + e]) - m_run));
+              q4[e] = f2tf32(ex2_approx(fmaf(__uint_as_float(rx[4 * k + e]), sl2, -m_run)));
               lsum += __uint_as_float(q4[e]);
             }
             *reinterpret_cast<uint4*>(xx + p_offset(2 * grp + k, row)) = make_uint4(q4[0], q4[1], q4[2], q4[3]);
@@ -758,8 +814,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
           uint32_t h4[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const __half2 hv = __floats2half2_rn(ex2_approx(__uint_as_float(rx[2 * e]) - m_run),
-                                                 ex2_approx(__uint_as_float(rx[2 * e + 1]) - m_run));
+            const __half2 hv = __floats2half2_rn(ex2_approx(fmaf(__uint_as_float(rx[2 * e]), sl2, -m_run)),
+                                                 ex2_approx(fmaf(__uint_as_float(rx[2 * e + 1]), sl2, -m_run)));
             const float2 back = __half22float2(hv);
             lsum += back.x + back.y;
             h4[e] = *reinterpret_cast<const uint32_t*>(&hv);
@@ -787,21 +843,28 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
     named_bar_sync(2 + quad, 32 * kGroups);  // red is rewritten by the next tile
     const int grow = row0 + row;
     const bool live = grow < p.n_latent;
-    if (ok && w.n_tiles > 0 &&
-        (ok = warp_mbar_wait(smem_u32(&bars.o_done), it & 1, kTimeoutMmaDone, abort))) {
+    // the next item's truncation factors (acquired now, used at its first tile)
+    if (comp && ok && w.n_tiles > 0 && with_tiles(item + n_clusters) < p.n_items)
+      ok = warp_mbar_wait<true>(smem_u32(&bars.stats_full[(it + 1) & 1]), static_cast<uint32_t>((it + 1) >> 1) & 1u,
+                                kTimeoutSoftmax, abort);
+    const bool have_o = ok && w.n_tiles > 0 &&
+                        (ok = warp_mbar_wait(smem_u32(&bars.o_done), it & 1, kTimeoutMmaDone, abort));
+    if (have_o) {
       if (sw == 0 && lane == 0) XATTN_TRACE_POINT(11, it);
       tc_fence_after();
+      // output factor of the item (tfac[it % 2] is refilled only after the arrival below)
+      const float oc = comp ? p.out_comp * tfac[it & 1][1] : p.out_comp;
       float scale;
       if (p.split_mode) {
         const float f = ex2_approx(m_run - m_true);
-        scale = f * p.out_comp;
+        scale = f * oc;
         const size_t pidx = (static_cast<size_t>(b) * p.n_latent + grow) * p.num_splits + split;
         if (live && h == 0 && grp == 0) {
           p.pm[pidx] = m_true * 0.69314718055994531f;
           p.pl[pidx] = l_tot * f;
         }
       } else {
-        scale = p.out_comp / l_tot;
+        scale = oc / l_tot;
       }
       // o_done (a multicast commit after the item's last P.V) means every P.V of the item
       // completed: the slot of the item's last piece, which the D-peer refills only after
@@ -836,6 +899,10 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         named_bar_sync(1, kSoftmaxThreads);
         if (sw == 0 && lane == 0)
           mbar_arrive_remote(peer_x_empty0 + ((U + w.uses() - 1) % kXSlots) * 8);
+      }
+      if (comp) {  // this warp is done with tfac[it % 2] (both factors were consumed above)
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(stats_empty0 + (it & 1) * 8);
       }
       g += w.n_tiles;
       U += w.uses();

@@ -101,6 +101,14 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar, uint32_
                : "memory");
 }
 
+// Arrive on a (possibly peer) mbarrier and raise its expected transaction count by `bytes`,
+// which st.async / bulk copies aimed at it then count down.  The phase completes once both
+// the arrivals and the bytes are in, in either order.
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(cluster_bar), "r"(bytes)
+               : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -219,6 +227,15 @@ __device__ __forceinline__ void st_async_v4(uint32_t cluster_addr, uint32_t clus
           cluster_addr),
       "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
       : "memory");
+}
+
+// Asynchronous 8-byte store into a CTA of the cluster (this one included), counted on that
+// CTA's mbarrier like st_async_v4.
+__device__ __forceinline__ void st_async_v2(uint32_t cluster_addr, uint32_t cluster_bar, float a, float b) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v2.f32 [%0], {%1, %2}, [%3];" ::"r"(
+                   cluster_addr),
+               "f"(a), "f"(b), "r"(cluster_bar)
+               : "memory");
 }
 
 __device__ __forceinline__ void cluster_sync() {

@@ -220,13 +220,22 @@ bool make_out_map(fused::Params& p, float* out, float* po, int B, int Nl, int D,
                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-// Score scale and TF32 compensation of a launch.  score_scale < 0 means 1/sqrt(D); exact
-// inputs (already representable in TF32, e.g. widened fp16) take no truncation compensation.
-void set_scale(fused::Params& p, int D, float score_scale, bool exact_inputs) {
+// Score scale and TF32 truncation compensation of a launch.  score_scale < 0 means
+// 1/sqrt(D).  Option 4 (default 1): the kernels measure the relative truncation of the
+// inputs on a sample per item and compensate exactly that (nothing for inputs already exact
+// in TF32); 2: the fixed statistical constants for random mantissas, whatever the inputs;
+// 0: no compensation.  Known-exact inputs (widened fp16) take none.
+void set_scale(fused::Params& p, const float* Q, const float* K, const float* V, int D,
+               float score_scale, bool exact_inputs) {
   const double sc = score_scale < 0.f ? 1.0 / std::sqrt(static_cast<double>(D)) : score_scale;
-  const bool comp = !exact_inputs && g_opt_tf32_comp.load() != 0;
-  p.scale_log2 = static_cast<float>(kLog2e * sc * (comp ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
-  p.out_comp = comp ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+  const int mode = exact_inputs ? 0 : g_opt_tf32_comp.load();
+  const bool fixed = mode == 2;
+  p.comp_mode = mode == 1 && Q != nullptr ? 1 : 0;
+  p.scale_log2 = static_cast<float>(kLog2e * sc * (fixed ? 1.0 + 2.0 * kTf32TruncBias : 1.0));
+  p.out_comp = fixed ? static_cast<float>(1.0 + kTf32TruncBias) : 1.f;
+  p.q = Q;
+  p.k = K;
+  p.v = V;
 }
 
 // Launch the fused kernel.  split_mode = 0: normalised output `out`; 1: partials.
@@ -261,7 +270,7 @@ int launch_fused(const float* Q, const float* K, const float* V, float* out, flo
   p.num_splits = num_splits;
   p.split_chunk = split_chunk;
   p.split_mode = split_mode;
-  set_scale(p, D, score_scale, exact_inputs);
+  set_scale(p, Q, K, V, D, score_scale, exact_inputs);
   const long long items = static_cast<long long>(B) * p.n_row_blocks * num_splits;
   if (items * 2 > 0x7fffffffLL) return XATTN_ERR_ARG;
   p.n_items = static_cast<int>(items);
@@ -321,7 +330,10 @@ int launch_fused_pair(const T* Q, const T* K, const T* V, float* out, float* po,
   p.num_splits = num_splits;
   p.split_chunk = split_chunk;
   p.split_mode = split_mode;
-  set_scale(p, D, score_scale, exact_inputs);
+  if constexpr (sizeof(T) == 4)
+    set_scale(p, Q, K, V, D, score_scale, exact_inputs);
+  else
+    set_scale(p, nullptr, nullptr, nullptr, D, score_scale, true);  // fp16 operands are exact
   const long long items = static_cast<long long>(B) * p.n_row_blocks * num_splits;
   if (items * 4 > 0x7fffffffLL) return XATTN_ERR_ARG;
   p.n_items = static_cast<int>(items);

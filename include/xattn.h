@@ -175,9 +175,12 @@ int xattn_status(int clear);
  * (no automatic key split), 2 CUDA-core generic kernel.  key 2 = forced number of key
  * splits for the automatic fp32 path (0 = heuristic).  key 3 = device wait bound in
  * microseconds (default 2,000,000).  key 4 = TF32 truncation-bias compensation of the
- * tensor-core fp32 path: 1 (default) scales scores by (1 + 2e) and the output by (1 + e),
- * e = 2^-11 / (2 ln 2), the mean relative truncation error of one operand; 0 turns it
- * off (for inputs already exact in TF32).  key 5 = fp32 tensor-core kernel: 0 auto, 1 the
+ * tensor-core fp32 path (the tensor cores truncate fp32 operands to 10 mantissa bits):
+ * 1 (default) measures, per work item, the least-squares relative truncation e_Q, e_K,
+ * e_V of a sample of the inputs and scales the scores by (1 + e_Q + e_K) and the output
+ * by (1 + e_V) -- exactly no compensation for inputs already exact in TF32 (widened bf16
+ * or fp16, small integers); 2 applies the fixed constants for random mantissas,
+ * e = 2^-11 / (2 ln 2) per operand, whatever the inputs; 0 turns it off.  key 5 = fp32 tensor-core kernel: 0 auto, 1 the
  * two-CTA kernel, 2 the four-CTA pair kernel (where the shape allows it).  key 6 = accurate
  * fp32 mode: 1 makes the non-split fp32 entries compute with 3xTF32 on the tensor cores
  * (two 3xTF32 GEMMs around an exact row softmax; max|dO| <= 1e-5 * max|O|; workspace of

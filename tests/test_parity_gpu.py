@@ -256,6 +256,95 @@ def test_batch_boundary_isolation(X, torch_cuda):
     assert_close(torch, out[0:1], ref_attention(torch, q[0:1], k[0:1], v[0:1]), TF32_TOL, "batch0")
 
 
+def _exact_class(torch, kind, shape, gen):
+    """fp32 tensors whose values are exactly representable in TF32."""
+    x = torch.randn(*shape, device="cuda", generator=gen)
+    if kind == "bf16":
+        return x.bfloat16().float()
+    if kind == "fp16":
+        return x.half().float()
+    if kind == "int":  # small integers, as from quantised or count data
+        return torch.randint(-4, 5, shape, device="cuda", generator=gen).float()
+    if kind == "tf32":  # rounded to TF32 (10 mantissa bits)
+        return ((x.view(torch.int32) + 0x1000) & -0x2000).view(torch.float32)
+    raise ValueError(kind)
+
+
+EXACT_SHAPES = [(1, 64, 784, 768), (32, 1024, 784, 768), (2, 300, 1000, 512), (3, 130, 200, 320)]
+
+
+@pytest.mark.parametrize("kind", ["bf16", "fp16", "int", "tf32"])
+@pytest.mark.parametrize("shape", EXACT_SHAPES, ids=lambda s: "B%d_Nl%d_Ni%d_D%d" % s)
+def test_tf32_exact_inputs_default_options(X, torch_cuda, kind, shape):
+    """Inputs already exact in TF32 (bf16- or fp16-upcast data, small integers) through the
+    default fp32 path: the measured truncation compensation finds nothing to correct, so the
+    result is bit-identical to compensation off, and within 2e-3 * max|O_ref| of float64.
+    C1 (key splits + combine), C3 (persistent pair kernel), D = 512 (pair kernel) and
+    D = 320 (two-CTA kernel)."""
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    gen = torch.Generator(device="cuda").manual_seed(sum(shape) + 1000 * "bf16 fp16 int tf32".split().index(kind))
+    q, k, v = (_exact_class(torch, kind, (b, n, d), gen) for n in (nl, ni, ni))
+    assert X.set_option(X.OPT_TF32_COMP, 1) == 1  # the default
+    out = X.cross_attention(q, k, v)
+    prev = X.set_option(X.OPT_TF32_COMP, 0)
+    try:
+        off = X.cross_attention(q, k, v)
+        torch.cuda.synchronize()
+    finally:
+        X.set_option(X.OPT_TF32_COMP, prev)
+    assert torch.equal(out, off), "compensation applied to inputs that TF32 represents exactly"
+    if b * nl * ni * d > 1e9:  # C3: float64 reference on the first two batches
+        q, k, v, out = q[:2], k[:2], v[:2], out[:2]
+    err = assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, f"{kind} {shape}")
+    if kind in ("bf16", "fp16", "tf32"):  # unit-scale data: the upstream drivers' 1e-3 absolute
+        assert err <= 1e-3
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int"])
+def test_tf32_exact_inputs_through_upstream_entry(X, torch_cuda, kind):
+    """launch_optimized_kernel with default options on TF32-exact inputs (C1 shape)."""
+    import ctypes
+
+    torch = torch_cuda
+    b, nl, ni, d = 1, 64, 784, 768
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    q, k, v = (_exact_class(torch, kind, (b, n, d), gen) for n in (nl, ni, ni))
+    out = torch.zeros_like(q)
+    lib = X.lib()
+    lib.launch_optimized_kernel.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 4 + [ctypes.c_void_p]
+    lib.launch_optimized_kernel(q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), b, nl, ni, d, None)
+    torch.cuda.synchronize()
+    assert lib.xattn_last_error() == 0
+    assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, f"upstream entry, {kind}")
+
+
+@pytest.mark.parametrize("shape", [(1, 64, 784, 768), (8, 1024, 784, 768), (3, 130, 200, 320)],
+                         ids=lambda s: "B%d_Nl%d_Ni%d_D%d" % s)
+def test_measured_compensation_on_mixed_inputs(X, torch_cuda, shape):
+    """Random fp32 data (every mantissa bit set at random), alone and mixed with TF32-exact
+    operands: the measured compensation keeps every mix within tolerance, and on pure
+    random data it is at least as accurate as no compensation."""
+    torch = torch_cuda
+    b, nl, ni, d = shape
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    rnd = [torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni)]
+    ex = [x.bfloat16().float() for x in rnd]
+    errs = {}
+    for label, ops in (("random", rnd), ("q exact", [ex[0], rnd[1], rnd[2]]),
+                       ("v exact", [rnd[0], rnd[1], ex[2]]), ("k,v exact", [rnd[0], ex[1], ex[2]])):
+        ref = ref_attention(torch, *ops)
+        errs[label] = assert_close(torch, X.cross_attention(*ops), ref, TF32_TOL, label)
+    prev = X.set_option(X.OPT_TF32_COMP, 0)
+    try:
+        off = X.cross_attention(*rnd)
+        torch.cuda.synchronize()
+    finally:
+        X.set_option(X.OPT_TF32_COMP, prev)
+    err_off = (off - ref_attention(torch, *rnd)).abs().max().item()
+    assert errs["random"] <= err_off
+
+
 def test_tf32_exact_inputs_without_compensation(X, torch_cuda):
     torch = torch_cuda
     q, k, v = (torch.randn(2, 128, 768, device="cuda") for _ in range(3))
