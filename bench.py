@@ -28,7 +28,6 @@ import math
 import os
 import statistics
 import sys
-import threading
 import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
@@ -81,63 +80,91 @@ def committed_traffic():
 
 
 # --------------------------------------------------------------------------- clocks
+# The sampler runs as its own process (a thread of this one starves on the GIL while the
+# main thread launches and synchronises): NVML every ~0.25 ms, one "t sm reasons" line per
+# sample on stdout, wall-clock timestamps comparable with time.time() here.
+_SAMPLER = r"""
+import sys, time, pynvml
+pynvml.nvmlInit()
+h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+out = []
+try:
+    while True:
+        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+        out.append("%.6f %d %d" % (time.time(), sm, r))
+        if len(out) >= 512:
+            sys.stdout.write("\n".join(out) + "\n"); sys.stdout.flush(); out = []
+        time.sleep(0.00025)
+except (KeyboardInterrupt, BrokenPipeError):
+    pass
+finally:
+    if out:
+        sys.stdout.write("\n".join(out) + "\n"); sys.stdout.flush()
+"""
+
+
 class ClockSampler:
-    """Samples SM clock, power and clock-event reasons via NVML every `period` seconds."""
+    """SM clock and clock-event reasons sampled by a separate process during the run."""
 
     REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
                0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, pci_bus_id, period=0.002):
-        self.samples, self.period, self.ok = [], period, False
-        self._stop = threading.Event()
+    def __init__(self, pci_bus_id):
+        import signal
+        import subprocess
+
+        self.signal = signal
+        self.max_mhz, self.proc = None, None
         try:
-            import pynvml
-
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = pynvml.nvmlDeviceGetHandleByPciBusId(pci_bus_id)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
-            self.ok = True
+            self.proc = subprocess.Popen([sys.executable, "-c", _SAMPLER, pci_bus_id],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            first = self.proc.stdout.readline().split()
+            self.max_mhz = int(first[1]) if len(first) == 2 and first[0] == "max" else None
+            if self.max_mhz is None:
+                self.proc.kill()
+                self.proc = None
         except Exception:
-            self.max_mhz = None
-
-    def _run(self):
-        nv = self.nv
-        while not self._stop.is_set():
-            try:
-                sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
-                t = time.time()
-                reasons = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append((t, sm, reasons))
-            except Exception:
-                pass
-            time.sleep(self.period)
-
-    def start(self):
-        if self.ok:
-            self.t = threading.Thread(target=self._run, daemon=True)
-            self.t.start()
+            self.proc = None
 
     def stop(self, t0, t1):
-        if not self.ok:
+        if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvml unavailable"]}
-        self._stop.set()
-        self.t.join(timeout=2)
-        inside = [s for s in self.samples if t0 <= s[0] <= t1] or self.samples[-3:]
+        self.proc.send_signal(self.signal.SIGINT)
+        text, _ = self.proc.communicate(timeout=10)
+        samples = []
+        for line in text.splitlines():
+            f = line.split()
+            if len(f) == 3:
+                samples.append((float(f[0]), int(f[1]), int(f[2])))
+        inside = [x for x in samples if t0 <= x[0] <= t1]
         reasons = set()
         for _, _, r in inside:
             for bit, name in self.REASONS.items():
                 if r & bit:
                     reasons.add(name)
-        return {"sm_mhz": statistics.median(s[1] for s in inside) if inside else None,
+        return {"sm_mhz": statistics.median(x[1] for x in inside) if inside else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(reasons),
-                "samples_in_timed_region": sum(1 for s in self.samples if t0 <= s[0] <= t1)}
+                "samples_in_timed_region": len(inside), "sampler": "NVML, own process, ~0.25 ms"}
 
 
-# --------------------------------------------------------------------------- reference arm
-def run_reference(args, rank):
-    if rank != 0:
-        return
+# --------------------------------------------------------------------------- CPU reference
+def workload_config(world):
+    """The `config` of both arms' JSON lines (same keys and values)."""
+    return {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world, "n_latent": NL,
+            "n_input": NI, "dim": D,
+            "l2": "inputs 355 MB per GPU > 126 MB L2; no flush needed"}
+
+
+def cpu_reference(steps, warmup, budget_s, target_s=None):
+    """The upstream CPU path (torch bmm / softmax / bmm, generate_batch_references.py:20-26,
+    restated in oracle/xattn_oracle.py) on all host threads, on the bench workload: seed-42
+    iid N(0,1) inputs of B=32, N_latent=1024, N_input=784, D=768.  Each step is the full
+    32-batch workload when `steps + warmup` of them fit `budget_s`, else the same leading
+    batch subset every step (throughput per batch is what is compared).  With `target_s`,
+    `steps` grows (at least the given number) to fill about that many seconds.  Returns
+    (TFLOP/s, seconds per full workload, threads, sample description)."""
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     import numpy as np
     import torch
@@ -150,30 +177,39 @@ def run_reference(args, rank):
     q = rng.standard_normal((B, NL, D), dtype=np.float32)
     k = rng.standard_normal((B, NI, D), dtype=np.float32)
     v = rng.standard_normal((B, NI, D), dtype=np.float32)
-    # Size each step so the whole run stays within ~3 minutes: the full workload when it
-    # fits, else a batch subset (same per-batch work, throughput scales exactly).
     t = time.perf_counter()
     orc.cross_attention_torch(q[:1], k[:1], v[:1], D)
     per_batch = time.perf_counter() - t
-    budget = 150.0 / max(1, args.steps + args.warmup)
-    nb = max(1, min(B, int(budget / max(per_batch, 1e-6))))
-    for _ in range(args.warmup):
+    nb = max(1, min(B, int(budget_s / max(1, steps + warmup) / max(per_batch, 1e-6))))
+    if target_s is not None:
+        steps = max(steps, int(target_s / max(per_batch * nb, 1e-6)))
+    for _ in range(warmup):
         orc.cross_attention_torch(q[:nb], k[:nb], v[:nb], D)
     times = []
-    for _ in range(args.steps):
+    for _ in range(steps):
         t = time.perf_counter()
         orc.cross_attention_torch(q[:nb], k[:nb], v[:nb], D)
         times.append(time.perf_counter() - t)
     sec = statistics.mean(times)
     tflops = 4.0 * nb * NL * NI * D / sec / 1e12
-    sample = f"{nb} of {B} batches per step ({'full workload' if nb == B else 'batch subset'})"
+    sample = (f"{steps} timed steps after {warmup} warm-up of {nb} of the {B} batches "
+              f"({'the full workload' if nb == B else 'a batch subset'}), seed 42")
+    return tflops, sec * B / nb, threads, sample
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    tflops, sec_full, threads, sample = cpu_reference(args.steps, args.warmup, 150.0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     line = {
         "metric": METRIC, "value": tflops, "unit": "TFLOP/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sec * 1e3 * B / nb, "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": sec_full * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic iid N(0,1) fp32, seed 42",
-        "config": {"workload": WORKLOAD, "batch_per_step": nb, "n_latent": NL, "n_input": NI,
-                   "dim": D, "path": "torch CPU bmm/softmax/bmm (upstream reference path)"},
+        "config": workload_config(world),
+        "path": "torch CPU bmm/softmax/bmm on the host cores (upstream reference path)",
         "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
@@ -183,28 +219,9 @@ def run_reference(args, rank):
 
 
 def cpu_baseline_sample():
-    """Upstream CPU path on the host cores, ~10 s bounded sample of the workload."""
-    sys.path.insert(0, os.path.join(REPO, "oracle"))
-    import numpy as np
-    import torch
-
-    import xattn_oracle as orc
-
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    rng = np.random.default_rng(0)
-    nb = 4
-    q = rng.standard_normal((nb, NL, D), dtype=np.float32)
-    k = rng.standard_normal((nb, NI, D), dtype=np.float32)
-    v = rng.standard_normal((nb, NI, D), dtype=np.float32)
-    orc.cross_attention_torch(q, k, v, D)
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < 10.0:
-        orc.cross_attention_torch(q, k, v, D)
-        n += 1
-    sec = (time.perf_counter() - t0) / n
-    return {"value": 4.0 * nb * NL * NI * D / sec / 1e12, "unit": "TFLOP/s", "cores": threads,
-            "kind": "port", "sample": f"{n} repetitions of {nb} of the {B} batches (~10 s)"}
+    """The reference arm's measurement, bounded to ~10 s: same workload, seed and threads."""
+    tflops, _, threads, sample = cpu_reference(steps=3, warmup=1, budget_s=30.0, target_s=10.0)
+    return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample}
 
 
 # --------------------------------------------------------------------------- our arm
@@ -260,8 +277,7 @@ def main():
 
     props = torch.cuda.get_device_properties(dev)
     pci = "%08X:%02X:%02X.0" % (props.pci_domain_id, props.pci_bus_id, props.pci_device_id)
-    sampler = ClockSampler(pci)
-    sampler.start()
+    sampler = ClockSampler(pci)  # running from here to the end of the timed region
 
     for _ in range(args.warmup):
         step()
@@ -336,11 +352,8 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "tf32",
             "data": "synthetic iid N(0,1) fp32 generated on device, seed 42+rank",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world,
-                       "n_latent": NL, "n_input": NI, "dim": D,
-                       "parallelism": f"row shards over {world} GPU(s), no collective",
-                       "key_splits": splits,
-                       "l2": "inputs 355 MB per GPU > 126 MB L2; no flush needed"},
+            "config": workload_config(world),
+            "parallelism": f"row shards over {world} GPU(s), no collective", "key_splits": splits,
             "gpu_launches": launches * args.steps,
             "roofline": roofline,
             "e2e": e2e,

@@ -70,8 +70,14 @@ def _record(store, key, q, k, v, out, full=False):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("XATTN_UPSTREAM", "/root/reference"))
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(HERE)), "oracle"))
+    import upstream
+
+    ap.add_argument("--ref", default=upstream.upstream_dir(),
+                    help="upstream checkout (default: XATTN_UPSTREAM, else ../reference)")
     args = ap.parse_args()
+    if args.ref is None:
+        ap.error("upstream checkout not found: pass --ref or set XATTN_UPSTREAM")
     sys.path.insert(0, args.ref)
 
     gen1 = _load(os.path.join(args.ref, "generate_references.py"), "up_generate_references")

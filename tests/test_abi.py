@@ -101,11 +101,19 @@ def test_mirror_wrapper_imports_and_binds_all_upstream_names():
         assert callable(getattr(cw, name))
 
 
-@pytest.mark.skipif(not os.path.isdir("/root/reference"), reason="upstream checkout not present")
+def _upstream_wrapper_dir():
+    import upstream  # oracle/upstream.py (conftest puts oracle/ on the path)
+
+    if os.path.isfile(os.path.join(upstream.STAGED, "cuda_wrappers.py")):
+        return upstream.STAGED
+    return upstream.upstream_dir()
+
+
+@pytest.mark.skipif(_upstream_wrapper_dir() is None, reason="upstream wrapper neither staged nor found")
 def test_upstream_wrapper_binds_this_library_unchanged(tmp_path):
     """Import the upstream cuda_wrappers.py itself against this kernels.so (no GPU calls)."""
     code = (
-        "import sys; sys.path.insert(0, '/root/reference'); import cuda_wrappers as cw;"
+        f"import sys; sys.path.insert(0, {_upstream_wrapper_dir()!r}); import cuda_wrappers as cw;"
         "assert cw.HAS_WMMA and cw.HAS_SPLITK and cw.HAS_WMMA_SPLITK;"
         "print(sorted(cw.LAUNCHERS))"
     )
