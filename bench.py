@@ -14,6 +14,11 @@ on the data path, weak scaling; the time is the max over ranks of CUDA-event tim
          the timed region, every step; the call pipelines batch chunks so the copy-in, the
          kernels and the copy-out of neighbouring chunks overlap.
 `roofline`, `cpu_baseline`, `clocks`, `gpu_launches` as the contract describes.
+`input_split` config 4 (B=8, N_latent=512, N_input=65536, D=768) with N_input split over
+         the N ranks: per-rank partial, the one-kernel peer-memory merge (and, for
+         comparison, the same merge as NCCL collectives), the whole step as the max over
+         ranks of CUDA-event time, and sampled rows against float64 (N=1: the single-GPU
+         path, no merge).
 
 `--impl reference` times the upstream project's own CPU path (torch bmm/softmax/bmm,
 generate_batch_references.py:20-26) restated in oracle/xattn_oracle.py, on all host
@@ -84,24 +89,20 @@ def committed_traffic():
 # main thread launches and synchronises): NVML every ~0.25 ms, one "t sm reasons" line per
 # sample on stdout, wall-clock timestamps comparable with time.time() here.
 _SAMPLER = r"""
-import sys, time, pynvml
+import signal, sys, time, pynvml
+stop = []
+signal.signal(signal.SIGINT, lambda *a: stop.append(1))  # only a flag: no write is cut short
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
 print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
 out = []
-try:
-    while True:
-        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
-        r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
-        out.append("%.6f %d %d" % (time.time(), sm, r))
-        if len(out) >= 512:
-            sys.stdout.write("\n".join(out) + "\n"); sys.stdout.flush(); out = []
-        time.sleep(0.00025)
-except (KeyboardInterrupt, BrokenPipeError):
-    pass
-finally:
-    if out:
-        sys.stdout.write("\n".join(out) + "\n"); sys.stdout.flush()
+while not stop:
+    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+    out.append("%.6f %d %d" % (time.time(), sm, r))
+    time.sleep(0.00025)
+sys.stdout.write("\n".join(out) + "\n")
+sys.stdout.flush()
 """
 
 
@@ -135,9 +136,11 @@ class ClockSampler:
         text, _ = self.proc.communicate(timeout=10)
         samples = []
         for line in text.splitlines():
-            f = line.split()
-            if len(f) == 3:
-                samples.append((float(f[0]), int(f[1]), int(f[2])))
+            try:
+                t, sm, r = line.split()
+                samples.append((float(t), int(sm), int(r)))
+            except ValueError:
+                continue
         inside = [x for x in samples if t0 <= x[0] <= t1]
         reasons = set()
         for _, _, r in inside:
@@ -222,6 +225,85 @@ def cpu_baseline_sample():
     """The reference arm's measurement, bounded to ~10 s: same workload, seed and threads."""
     tflops, _, threads, sample = cpu_reference(steps=3, warmup=1, budget_s=30.0, target_s=10.0)
     return {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample}
+
+
+# --------------------------------------------------------------------------- config 4
+def input_split_record(xattn, torch, dist, world, rank, dev, steps=10, warmup=3):
+    """Config 4 with N_input split over the ranks: every rank holds all of Q (~N(0,1)) and a
+    contiguous slice of the 65536 keys (K, V ~ N(0, 0.5^2)), generated in chunks of 4096 keys
+    from per-chunk seeds so that rank 0 can regenerate the whole K/V for the check."""
+    b, nl, ni, d = 8, 512, 65536, 768
+    lo, hi = xattn.shard_rows(ni, rank, world)
+
+    def slice_kv(lo_, hi_):
+        ks, vs = [], []
+        for c0 in range(lo_ // 4096 * 4096, hi_, 4096):
+            g = torch.Generator(device=dev).manual_seed(1000 + c0 // 4096)
+            kc = torch.randn(b, 4096, d, device=dev, generator=g) * 0.5
+            vc = torch.randn(b, 4096, d, device=dev, generator=g) * 0.5
+            s0, s1 = max(lo_, c0) - c0, min(hi_, c0 + 4096) - c0
+            ks.append(kc[:, s0:s1])
+            vs.append(vc[:, s0:s1])
+        return torch.cat(ks, 1).contiguous(), torch.cat(vs, 1).contiguous()
+
+    q = torch.randn(b, nl, d, device=dev, generator=torch.Generator(device=dev).manual_seed(4))
+    k, v = slice_kv(lo, hi)
+    ex = xattn.PeerExchange(b, nl, d) if world > 1 else None
+    single = torch.empty_like(q)
+
+    def step():
+        if ex is None:
+            xattn.cross_attention(q, k, v, out=single)
+            return single
+        ex.partial(q, k, v)
+        return ex.merge()
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            fn()
+        e1.record()
+        e1.synchronize()
+        return e0.elapsed_time(e1) / steps * 1e3  # us
+
+    t = [timed(step)]
+    out = step().clone()
+    if ex is not None:
+        t.append(timed(lambda: ex.partial(q, k, v)))
+        t.append(timed(ex.merge))
+        po, pm, pl = ex.po.clone(), ex.pm.clone(), ex.pl.clone()
+        t.append(timed(lambda: xattn.merge_input_split(po, pm, pl)))
+    tt = torch.tensor(t, device=dev)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ex.close()
+    rec = None
+    if rank == 0:
+        kf, vf = slice_kv(0, ni)
+        rows = torch.arange(0, nl, 53, device=dev)
+        worst = 0.0
+        for i in range(b):
+            ref = torch.softmax(q[i, rows].double() @ kf[i].double().T / math.sqrt(d), -1) @ vf[i].double()
+            worst = max(worst, (out[i, rows].double() - ref).abs().max().item() / ref.abs().max().item())
+        del kf, vf
+        t = tt.tolist()
+        flops = 4.0 * b * nl * ni * d
+        rec = {"config": "config 4: B=8 N_latent=512 N_input=65536 D=768, K,V ~ N(0, 0.5^2)",
+               "split": f"N_input over {world} rank(s), {hi - lo} keys on rank 0",
+               "step_us": t[0], "value": flops / (t[0] * 1e-6) / 1e12, "unit": "TFLOP/s",
+               "steps": steps, "rel_err_sampled_rows": worst, "tolerance": 2e-3}
+        if world > 1:
+            rec.update({"partial_us": t[1], "merge_us": t[2], "merge_nccl_us": t[3],
+                        "merge": "one kernel per rank over NVLink peer memory (xattn_peer_merge)"})
+        if not worst <= 2e-3:
+            raise SystemExit(f"bench guard: config 4 rel err {worst:.3e} > 2e-3")
+    return rec
 
 
 # --------------------------------------------------------------------------- our arm
@@ -333,6 +415,9 @@ def main():
     e2e = {"value": flops_per_step() * world / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
            "ms_per_step": e2e_ms, "h2d_bytes_per_step": (hq.nbytes + hk.nbytes + hv.nbytes) * world,
            "d2h_bytes_per_step": hout.nbytes * world, "steps": args.e2e_steps}
+    del hq, hk, hv, hout, q, k, v, out
+    torch.cuda.empty_cache()
+    split_rec = input_split_record(xattn, torch, dist, world, rank, dev)
 
     if rank == 0:
         peaks = measured_peaks()
@@ -358,6 +443,7 @@ def main():
             "roofline": roofline,
             "e2e": e2e,
             "clocks": clocks,
+            "input_split": split_rec,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline_sample()

@@ -230,6 +230,19 @@ __global__ void __launch_bounds__(128) lse_pack_kernel(const float* __restrict__
   if (lane == 0) ol[r * (dim + 1) + dim] = pl[r];
 }
 
+// Empty partials (no keys in the range, upstream kernel_splitk.cu:62-71): pm = -FLT_MAX,
+// pl = 0, po = 0 for `n` (row, split) entries of `dim` columns.
+__global__ void __launch_bounds__(256) empty_partials_kernel(float* __restrict__ po, float* __restrict__ pm,
+                                                             float* __restrict__ pl, long long n, int dim) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    pm[i] = -3.4028234663852886e38f;
+    pl[i] = 0.f;
+  }
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n * dim; i += stride)
+    po[i] = 0.f;
+}
+
 // Widen fp16 to fp32 (exact: every fp16 value is representable in fp32, and in TF32), 8
 // elements per thread per step.  n8 = number of 8-element groups; in and out 16-byte aligned.
 __global__ void __launch_bounds__(256) widen_half_kernel(const uint4* __restrict__ in,

@@ -34,6 +34,7 @@ enum StatusCode : int {
   kTimeoutPeer = 6,
   kTimeoutDrain = 7,
   kMisalignedSmem = 8,  // dynamic shared memory not 1024-byte aligned (kernel did nothing)
+  kTimeoutRank = 9,     // a barrier among GPUs (peer merge) was not reached by every rank
   kTimeoutInjected = 99,
 };
 

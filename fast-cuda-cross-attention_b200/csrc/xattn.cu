@@ -18,6 +18,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -28,6 +29,7 @@
 #include "fused_tf32.cuh"
 #include "fused_tf32_pair.cuh"
 #include "mha_bf16.cuh"
+#include "peer.cuh"
 #include "simt.cuh"
 #include "sm100.cuh"
 #include "tmap.h"
@@ -469,6 +471,14 @@ int zero_output(float* O, int B, int Nl, int D, cudaStream_t stream) {
   return cudaMemsetAsync(O, 0, bytes, stream) == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
 }
 
+// Partials of key ranges without keys: (-FLT_MAX, 0, 0) for n (row, split) entries.
+int empty_partials(float* po, float* pm, float* pl, long long n, int D, cudaStream_t stream) {
+  if (n <= 0) return XATTN_OK;
+  const unsigned blocks = static_cast<unsigned>(std::min<long long>((n * D + 255) / 256, 148LL * 8));
+  simt::empty_partials_kernel<<<blocks, 256, 0, stream>>>(po, pm, pl, n, D);
+  return cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH;
+}
+
 // Key-split plan of the automatic fp32 path: one pass when batch * row blocks fill the
 // two-CTA cluster slots (SMs / 2), otherwise enough tile-aligned splits to fill them
 // (used for the two-CTA kernel; the pair kernel plans with plan_pair_splits).
@@ -649,12 +659,16 @@ int run_splitk(const float* Q, const float* K, const float* V, float* O, float* 
                float* pl, int B, int Nl, int Ni, int D, int S, cudaStream_t stream) {
   if (bad_sizes(B, Nl, Ni, D) || S <= 0) return set_error(XATTN_ERR_ARG);
   if (B == 0 || Nl == 0) return set_error(XATTN_OK);
-  if (Q == nullptr || K == nullptr || V == nullptr || O == nullptr || po == nullptr ||
-      pm == nullptr || pl == nullptr)
+  if (O == nullptr || po == nullptr || pm == nullptr || pl == nullptr ||
+      (Ni > 0 && (Q == nullptr || K == nullptr || V == nullptr)))  // no keys: K, V unused
     return set_error(XATTN_ERR_ARG);
   int dev = 0;
   int rc = prepare_device(&dev);
   if (rc != XATTN_OK) return set_error(rc);
+  if (Ni == 0) {  // every split empty: empty partials, zero output (what the combine gives)
+    rc = empty_partials(po, pm, pl, static_cast<long long>(B) * Nl * S, D, stream);
+    return set_error(rc != XATTN_OK ? rc : zero_output(O, B, Nl, D, stream));
+  }
   const int chunk = std::max(1, (Ni + S - 1) / S);  // kernel_splitk.cu:59
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(D));
   if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, O, D) || !aligned16(po))
@@ -829,9 +843,17 @@ extern "C" void launch_wmma_splitk_kernel(const __half* Q, const __half* K, cons
     return;
   }
   if (batch_size == 0 || N_latent == 0) { set_error(XATTN_OK); return; }
-  if (Q == nullptr || K == nullptr || V == nullptr || output == nullptr || po == nullptr ||
-      pm == nullptr || pl == nullptr) {
+  if (output == nullptr || po == nullptr || pm == nullptr || pl == nullptr ||
+      (N_input > 0 && (Q == nullptr || K == nullptr || V == nullptr))) {  // no keys: K, V unused
     set_error(XATTN_ERR_ARG);
+    return;
+  }
+  if (N_input == 0) {
+    int dev = 0;
+    int rc = prepare_device(&dev);
+    if (rc == XATTN_OK)
+      rc = empty_partials(po, pm, pl, static_cast<long long>(batch_size) * N_latent * num_splits, dim, stream);
+    set_error(rc != XATTN_OK ? rc : zero_output(output, batch_size, N_latent, dim, stream));
     return;
   }
   set_error(run_half(Q, K, V, output, po, pm, pl, batch_size, N_latent, N_input, dim, num_splits,
@@ -850,9 +872,12 @@ extern "C" int xattn_fp32_partial(const float* Q, const float* K, const float* V
                                   int N_input, int dim, cudaStream_t stream) {
   if (bad_sizes(batch_size, N_latent, N_input, dim)) return set_error(XATTN_ERR_ARG);
   if (batch_size == 0 || N_latent == 0) return set_error(XATTN_OK);
+  if (po == nullptr || pm == nullptr || pl == nullptr) return set_error(XATTN_ERR_ARG);
   int dev = 0;
   int rc = prepare_device(&dev);
   if (rc != XATTN_OK) return set_error(rc);
+  if (N_input == 0)  // a rank whose key slice is empty (N_input split over more ranks than keys)
+    return set_error(empty_partials(po, pm, pl, static_cast<long long>(batch_size) * N_latent, dim, stream));
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(dim));
   const int path = g_opt_path.load();
   if (path == 2 || !tc_fp32_supported(Q, K, V, po, dim))
@@ -955,7 +980,12 @@ extern "C" int xattn_bf16_mha(const __nv_bfloat16* Q, const __nv_bfloat16* K,
                               cudaStream_t stream) {
   if (bad_sizes(batch_size, N_latent, N_input, head_dim) || heads <= 0)
     return set_error(XATTN_ERR_ARG);
-  if (batch_size == 0 || N_latent == 0 || N_input == 0) return set_error(XATTN_OK);
+  if (batch_size == 0 || N_latent == 0) return set_error(XATTN_OK);
+  if (output == nullptr) return set_error(XATTN_ERR_ARG);
+  if (N_input == 0) {  // softmax over no keys: zeros, as for the fp32 entries
+    const size_t bytes = static_cast<size_t>(batch_size) * N_latent * heads * head_dim * sizeof(__nv_bfloat16);
+    return set_error(cudaMemsetAsync(output, 0, bytes, stream) == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+  }
   int dev = 0;
   int rc = prepare_device(&dev);
   if (rc != XATTN_OK) return set_error(rc);
@@ -1052,6 +1082,85 @@ extern "C" int xattn_selftest_timeout(int bound_us) {
 }
 
 extern "C" int xattn_version(void) { return kVersion; }
+
+// ===================================================================== multi-GPU peer merge
+extern "C" int xattn_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (ptr == nullptr || handle == nullptr || bytes == 0) return set_error(XATTN_ERR_ARG);
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(XATTN_ERR_NOMEM);
+  }
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(*ptr, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, *ptr) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return set_error(XATTN_ERR_LAUNCH);
+  }
+  static_assert(sizeof(h) == XATTN_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return set_error(XATTN_OK);
+}
+
+extern "C" int xattn_ipc_open(const void* handle, void** ptr) {
+  if (ptr == nullptr || handle == nullptr) return set_error(XATTN_ERR_ARG);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  if (cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    *ptr = nullptr;
+    return set_error(XATTN_ERR_LAUNCH);
+  }
+  return set_error(XATTN_OK);
+}
+
+extern "C" int xattn_ipc_close(void* ptr) {
+  return set_error(cudaIpcCloseMemHandle(ptr) == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+}
+
+extern "C" int xattn_ipc_free(void* ptr) {
+  return set_error(cudaFree(ptr) == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+}
+
+extern "C" long long xattn_peer_layout(long long rows, int dim, long long* offsets) {
+  if (rows < 0 || dim <= 0) return -1;
+  const peer::Layout l = peer::layout(rows, dim);
+  if (offsets != nullptr) {
+    offsets[0] = l.pm;
+    offsets[1] = l.pl;
+    offsets[2] = l.po;
+    offsets[3] = l.out;
+  }
+  return l.total * 4;
+}
+
+extern "C" int xattn_peer_merge(void* const* bases, int n_ranks, int rank, long long rows, int dim,
+                                unsigned int epoch, cudaStream_t stream) {
+  if (bases == nullptr || n_ranks < 1 || n_ranks > peer::kMaxRanks || rank >= n_ranks || rows < 0 ||
+      dim <= 0 || rows > 0x7fffffffLL)
+    return set_error(XATTN_ERR_ARG);
+  int dev = 0;
+  int rc = prepare_device(&dev);
+  if (rc != XATTN_OK) return set_error(rc);
+  peer::Params a = {};
+  for (int p = 0; p < n_ranks; ++p) {
+    if (bases[p] == nullptr || !aligned16(bases[p])) return set_error(XATTN_ERR_ARG);
+    a.base[p] = static_cast<float*>(bases[p]);
+  }
+  a.rows = rows;
+  a.dim = dim;
+  a.n_ranks = n_ranks;
+  a.rank = rank;
+  a.epoch = epoch;
+  a.lay = peer::layout(rows, dim);
+  const long long mine = rank < 0 ? rows : rows * (rank + 1) / n_ranks - rows * rank / n_ranks;
+  // a warp per row; at least one block, so that every rank takes part in both barriers
+  const long long want = (mine + peer::kThreads / 32 - 1) / (peer::kThreads / 32);
+  const unsigned blocks = static_cast<unsigned>(std::max<long long>(1, std::min<long long>(want, sm_count(dev) * 4LL)));
+  peer::merge_kernel<<<blocks, peer::kThreads, 0, stream>>>(a);
+  return set_error(cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+}
 
 #ifdef XATTN_TRACE
 // Development builds only: copies the device timeline buffer to `host` (16*16*16 u64).

@@ -16,8 +16,12 @@ Multi-GPU (one process per GPU, ``torch.distributed``):
 * ``shard_rows`` -- batch rows split contiguously over ranks; every rank runs the
   fused kernel on its own shard, no collective on the data path (weak scaling).
 * ``cross_attention_input_split`` -- N_input split over ranks: each rank computes the
-  partial (m, l, O) of its key slice, then ``merge_input_split`` does
-  all-reduce(MAX, m) -> rescale -> all-reduce(SUM, [O | l]) -> O / l over NCCL.
+  partial (m, l, O) of its key slice into a peer-mapped exchange buffer (``PeerExchange``,
+  CUDA IPC over NVLink) and ONE merge kernel per rank (``xattn_peer_merge``) exchanges and
+  merges the partials over peer memory and leaves every row on every rank.
+  ``merge_input_split`` is the same merge as NCCL collectives (all-reduce(MAX, m) ->
+  rescale -> all-reduce(SUM, [O | l]) -> O / l), for process groups without peer memory
+  (e.g. gloo) and as the comparison baseline.
 
 Roofline formulas follow ``experiments/roofline.py:25-36`` upstream:
 FLOPs = 4 B Nl Ni D, fused bytes = (2 Nl D + 2 Ni D) B elem.
@@ -45,7 +49,8 @@ EXPORTED = (
     "launch_wmma_splitk_kernel", "xattn_fp32", "xattn_fp32_partial", "xattn_combine",
     "xattn_lse_pack", "xattn_lse_rescale", "xattn_lse_finalize", "xattn_bf16_mha",
     "xattn_last_error", "xattn_status", "xattn_set_option", "xattn_selftest_timeout",
-    "xattn_version", "xattn_plan_fp32", "xattn_splitk_noalloc",
+    "xattn_version", "xattn_plan_fp32", "xattn_splitk_noalloc", "xattn_ipc_alloc", "xattn_ipc_open",
+    "xattn_ipc_close", "xattn_ipc_free", "xattn_peer_layout", "xattn_peer_merge",
 )
 
 OPT_PATH, OPT_SPLITS, OPT_WAIT_US, OPT_TF32_COMP, OPT_KERNEL, OPT_ACCURATE = 1, 2, 3, 4, 5, 6
@@ -82,6 +87,12 @@ def lib():
         "xattn_version": ([], i),
         "xattn_plan_fp32": ([i, i, i, i, ctypes.POINTER(i)], i),
         "xattn_splitk_noalloc": ([vp] * 4 + [i] * 5 + [vp], i),
+        "xattn_ipc_alloc": ([ctypes.c_size_t, ctypes.POINTER(vp), vp], i),
+        "xattn_ipc_open": ([ctypes.c_char_p, ctypes.POINTER(vp)], i),
+        "xattn_ipc_close": ([vp], i),
+        "xattn_ipc_free": ([vp], i),
+        "xattn_peer_layout": ([ll, i, ctypes.POINTER(ll)], ll),
+        "xattn_peer_merge": ([vp, i, i, ll, i, ctypes.c_uint, vp], i),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -362,7 +373,120 @@ def merge_input_split(po, pm, pl, group=None, ops: Optional[MergeOps] = None):
     return ops.finalize(ol).reshape(shape)
 
 
-def cross_attention_input_split(q, k_local, v_local, group=None):
-    """Attention over the union of every rank's key slice (N_input split across GPUs)."""
-    po, pm, pl = cross_attention_partial(q, k_local, v_local)
-    return merge_input_split(po, pm, pl, group)
+class _DeviceArray:
+    """Zero-copy torch view of device memory the library allocated."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": "<f4", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """Exchange buffers of the N_input split over peer memory, one per rank of `group`.
+
+    Every rank allocates its buffer (``xattn_ipc_alloc``), the 64-byte CUDA IPC handles go
+    round with ``all_gather_object`` and every rank maps every other rank's buffer
+    (``xattn_ipc_open``, NVLink peer access).  ``po`` / ``pm`` / ``pl`` are this rank's
+    partial-output views (written by ``xattn_fp32_partial``), ``out`` the merged result
+    [B, N_latent, D], valid until the next ``merge``.  One process per GPU of one node, at
+    most eight ranks.  ``rows`` = B * N_latent.
+    """
+
+    def __init__(self, b: int, nl: int, d: int, group=None):
+        import torch
+        import torch.distributed as dist
+
+        L = lib()
+        self.group, self.shape = group, (b, nl, d)
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the peer merge takes at most eight ranks")
+        self.rows, self.dim = b * nl, d
+        offs = (ctypes.c_longlong * 4)()
+        total = L.xattn_peer_layout(self.rows, d, offs)
+        local, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+        _raise(L.xattn_ipc_alloc(total, ctypes.byref(local), handle), "xattn_ipc_alloc")
+        self.local = local.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle.raw, group=group)
+        self.opened, ptrs = [], []
+        for p, h in enumerate(handles):
+            if p == self.rank:
+                ptrs.append(self.local)
+                continue
+            peer = ctypes.c_void_p()
+            _raise(L.xattn_ipc_open(h, ctypes.byref(peer)), "xattn_ipc_open")
+            self.opened.append(peer.value)
+            ptrs.append(peer.value)
+        self.bases = (ctypes.c_void_p * self.world)(*ptrs)
+        dev = torch.device("cuda", torch.cuda.current_device())
+
+        def view(off, shape):
+            return torch.as_tensor(_DeviceArray(self.local + int(off) * 4, shape), device=dev)
+
+        self.pm, self.pl = view(offs[0], (b, nl)), view(offs[1], (b, nl))
+        self.po, self.out = view(offs[2], (b, nl, d)), view(offs[3], (b, nl, d))
+        self.epoch = 0
+        torch.cuda.synchronize()  # the buffer is zeroed (flags at epoch 0) before any peer uses it
+        dist.barrier(group=group)
+
+    def partial(self, q, k_local, v_local):
+        """This rank's (m, l, O) over its keys, into the exchange buffer."""
+        q, k_local, v_local = _as3(q), _as3(k_local), _as3(v_local)
+        _check_fp32(q, k_local, v_local)
+        b, nl, d = q.shape
+        if (b, nl, d) != self.shape:
+            raise ValueError(f"exchange built for {self.shape}, got {(b, nl, d)}")
+        _raise(lib().xattn_fp32_partial(q.data_ptr(), k_local.data_ptr(), v_local.data_ptr(),
+                                        self.po.data_ptr(), self.pm.data_ptr(), self.pl.data_ptr(),
+                                        b, nl, k_local.shape[1], d, _stream()), "xattn_fp32_partial")
+
+    def merge(self):
+        """One kernel: wait for every rank's partials, merge this rank's rows over peer memory
+        into every rank's ``out``, wait for every rank.  Returns ``out``."""
+        self.epoch += 1
+        _raise(lib().xattn_peer_merge(self.bases, self.world, self.rank, self.rows, self.dim,
+                                      self.epoch, _stream()), "xattn_peer_merge")
+        return self.out
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # nobody reads or writes the buffers any more
+        L = lib()
+        for p in self.opened:
+            L.xattn_ipc_close(p)
+        dist.barrier(group=self.group)
+        L.xattn_ipc_free(self.local)
+        self.opened, self.local = [], None
+
+
+_EXCHANGES = {}
+
+
+def cross_attention_input_split(q, k_local, v_local, group=None, method: str = "peer"):
+    """Attention over the union of every rank's key slice (N_input split across GPUs).
+
+    method="peer": the partial into this rank's exchange buffer, then the one-kernel merge
+    over peer memory (``PeerExchange``, cached per shape and group; the returned tensor is
+    its ``out``, valid until the next call with that shape).  method="nccl": the merge as
+    NCCL collectives (``merge_input_split``), a new tensor."""
+    if method == "nccl":
+        po, pm, pl = cross_attention_partial(q, k_local, v_local)
+        return merge_input_split(po, pm, pl, group)
+    q = _as3(q)
+    key = (tuple(q.shape), group)
+    ex = _EXCHANGES.get(key)
+    if ex is None:
+        ex = _EXCHANGES[key] = PeerExchange(*q.shape, group=group)
+    ex.partial(q, k_local, v_local)
+    return ex.merge()
+
+
+def close_exchanges():
+    """Unmaps and frees every cached PeerExchange (collective: every rank calls it)."""
+    for ex in _EXCHANGES.values():
+        ex.close()
+    _EXCHANGES.clear()

@@ -164,6 +164,33 @@ int xattn_splitk_noalloc(const float* Q, const float* K, const float* V, float* 
                          int batch_size, int N_latent, int N_input, int dim, int num_splits,
                          cudaStream_t stream);
 
+/* ---- Multi-GPU N_input split over peer memory (no counterpart upstream; the single-GPU
+ * combine it generalises is kernel_splitk.cu:186-236).  One process per GPU of one node.
+ *
+ * Each rank allocates one exchange buffer with xattn_ipc_alloc, sends the 64-byte handle to
+ * the other ranks (any host channel) and maps theirs with xattn_ipc_open (CUDA IPC over
+ * NVLink; no multicast object).  The buffer layout for `rows` = B * N_latent rows of `dim`
+ * floats comes from xattn_peer_layout (offsets in floats: pm, pl, po, out).  Per call, a
+ * rank writes its partial (m, l, O) over its keys into pm / pl / po of its own buffer
+ * (xattn_fp32_partial) and then calls xattn_peer_merge with every rank's mapped base
+ * pointer (its own at index `rank`) and an epoch that grows by one per call (first call:
+ * 1).  That one kernel waits until every rank's partials are written, merges its share
+ * of the rows reading every rank's partials over NVLink, writes the merged rows into the
+ * out region of every rank, and waits until every rank has done the same: when it
+ * completes, out holds all rows on every rank and the buffers may be reused.  All ranks
+ * must call it with the same rows, dim and epoch.  A rank that never arrives makes the
+ * others give up after the device wait bound (status XATTN_ERR_DEVICE via xattn_status,
+ * device code 9).  rank = -1 merges all rows of n_ranks buffers of this GPU in one launch
+ * without barriers (single-process use and tests).                                      */
+#define XATTN_IPC_HANDLE_BYTES 64
+int xattn_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int xattn_ipc_open(const void* handle, void** ptr);
+int xattn_ipc_close(void* ptr);
+int xattn_ipc_free(void* ptr);
+long long xattn_peer_layout(long long rows, int dim, long long* offsets);
+int xattn_peer_merge(void* const* bases, int n_ranks, int rank, long long rows, int dim,
+                     unsigned int epoch, cudaStream_t stream);
+
 /* Host-side status of the most recent call on this thread (XATTN_* code).              */
 int xattn_last_error(void);
 

@@ -91,12 +91,15 @@ def dying_worker(rank, world, port, results):
 
 
 def nccl_split_worker(rank, world, port, results):
-    """One GPU rank of the NCCL N_input-split test (tests/test_multigpu.py).
+    """One GPU rank of the N_input-split test (tests/test_multigpu.py).
 
-    Holds all of Q and the rank's slice of K/V, merges through
-    xattn.cross_attention_input_split, and reports its errors (relative to max|O_ref|)
-    against the single-GPU result and a float64 reference; then computes an N_latent row
-    shard with no collective and reports that error too."""
+    Holds all of Q and the rank's slice of K/V.  Merges through
+    xattn.cross_attention_input_split with the one-kernel peer-memory merge three times in a
+    row on different data (the exchange buffers and epochs are reused), and once through the
+    NCCL collectives, and reports the errors (relative to max|O_ref|) of the peer result
+    against the NCCL result, the single-GPU result and float64; then a shape with only one
+    key, so every rank but one holds an empty key slice; then an N_latent row shard with no
+    collective."""
     import datetime
     import math
 
@@ -112,20 +115,34 @@ def nccl_split_worker(rank, world, port, results):
         import xattn
 
         b, nl, ni, d = 2, 200, 3000, 768
-        gen = torch.Generator(device="cuda").manual_seed(21)
-        q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
         lo, hi = xattn.shard_rows(ni, rank, world)
-        merged = xattn.cross_attention_input_split(q, k[:, lo:hi].contiguous(), v[:, lo:hi].contiguous())
-        full = xattn.cross_attention(q, k, v)
-        exact = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(d), -1) @ v.double()
-        scale = exact.abs().max().item()
+        worst = [0.0, 0.0, 0.0]
+        for seed in (21, 22, 23):
+            gen = torch.Generator(device="cuda").manual_seed(seed)
+            q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+            kl, vl = k[:, lo:hi].contiguous(), v[:, lo:hi].contiguous()
+            merged = xattn.cross_attention_input_split(q, kl, vl).clone()
+            via_nccl = xattn.cross_attention_input_split(q, kl, vl, method="nccl")
+            full = xattn.cross_attention(q, k, v)
+            exact = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(d), -1) @ v.double()
+            scale = exact.abs().max().item()
+            torch.cuda.synchronize()
+            for i, e in enumerate(((merged - via_nccl).abs().max().item() / scale,
+                                   (merged - full).abs().max().item() / scale,
+                                   (merged.double() - exact).abs().max().item() / scale)):
+                worst[i] = max(worst[i], e)
+        # one key: every rank except one has an empty slice (the (-FLT_MAX, 0, 0) partial)
+        q1 = torch.randn(b, 64, d, device="cuda", generator=gen)
+        k1 = torch.randn(b, 1, d, device="cuda", generator=gen)
+        l1, h1 = xattn.shard_rows(1, rank, world)
+        one = xattn.cross_attention_input_split(q1, k1[:, l1:h1].contiguous(), k1[:, l1:h1].contiguous())
+        e_one = (one - k1.expand(b, 64, d)).abs().max().item() / k1.abs().max().item()
         r0, r1 = xattn.shard_rows(nl, rank, world)
         rows = xattn.cross_attention(q[:, r0:r1].contiguous(), k, v)
         torch.cuda.synchronize()
-        errs = ((merged - full).abs().max().item() / scale,
-                (merged.double() - exact).abs().max().item() / scale,
-                (rows.double() - exact[:, r0:r1]).abs().max().item() / scale)
+        errs = tuple(worst) + (e_one, (rows.double() - exact[:, r0:r1]).abs().max().item() / scale)
         status = xattn.device_status()
+        xattn.close_exchanges()
         dist.barrier()
         dist.destroy_process_group()
         results.put((rank, errs, status, None))

@@ -24,7 +24,7 @@ UPSTREAM = ["launch_naive_kernel", "launch_parallel_kernel", "launch_tiled_kerne
 def declared_functions():
     text = open(HEADER).read()
     text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
-    return sorted(set(re.findall(r"^\s*(?:void|int)\s+(\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:void|int|long long)\s+(\w+)\s*\(", text, flags=re.M)))
 
 
 def exported_symbols():

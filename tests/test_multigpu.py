@@ -1,12 +1,14 @@
-"""N_input split across GPUs with the NCCL merge (needs two or more GPUs; skipped otherwise).
+"""N_input split across GPUs (needs two or more GPUs; skipped otherwise).
 
 Each of two ranks (one process per GPU, NCCL process group on 127.0.0.1) holds the full
 Q and half of the keys.  xattn.cross_attention_input_split computes the rank's partial
-(m, l, O) with the tensor-core partial kernel and merges them with all_reduce(MAX) on m
-and all_reduce(SUM) on the rescaled [O | l].  The merged output must match the
-single-GPU result over all keys within the TF32 tolerance (2e-3 * max|O_ref|), and a
-float64 reference.  The second part shards N_latent rows across the ranks (no collective)
-and checks each rank's slice the same way.
+(m, l, O) with the tensor-core partial kernel into a peer-mapped exchange buffer and merges
+the ranks' partials with one kernel per rank over NVLink peer memory (xattn_peer_merge),
+three calls in a row.  The result must equal the NCCL-collective merge (all_reduce(MAX) on
+m, all_reduce(SUM) on the rescaled [O | l]) to 1e-5, and match the single-GPU result over
+all keys and a float64 reference within the TF32 tolerance (2e-3 * max|O_ref|).  With one
+key in all, every rank but one holds an empty slice and the output is that key's value
+row.  The last part shards N_latent rows across the ranks (no collective).
 """
 
 import socket
@@ -52,7 +54,9 @@ def test_input_split_nccl_merge_two_gpus():
     for rank, errs, status, err in sorted(out, key=lambda x: x[0]):
         assert err is None, f"rank {rank}: {err}"
         assert status == 0
-        e_full, e_exact, e_rows = errs
+        e_nccl, e_full, e_exact, e_one, e_rows = errs
+        assert e_nccl <= 1e-5, f"rank {rank}: peer merge vs NCCL merge {e_nccl:.2e}"
         assert e_full <= TF32_TOL, f"rank {rank}: merged vs single-GPU {e_full:.2e}"
         assert e_exact <= TF32_TOL, f"rank {rank}: merged vs float64 {e_exact:.2e}"
+        assert e_one <= TF32_TOL, f"rank {rank}: one key, empty slices {e_one:.2e}"
         assert e_rows <= TF32_TOL, f"rank {rank}: row shard {e_rows:.2e}"

@@ -633,6 +633,75 @@ def test_input_split_merge_kernels_single_gpu(X, torch_cuda):
     assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, "merge")
 
 
+def test_peer_merge_kernel_single_gpu_emulation(X, torch_cuda):
+    """xattn_peer_merge with rank = -1: one launch merges every row of three exchange
+    buffers of this GPU without the barriers -- the arithmetic and buffer layout of the
+    multi-GPU N_input split's one-kernel merge, on a ragged split with an empty key slice
+    (its partial is the (-FLT_MAX, 0, 0) triple xattn_fp32_partial writes for no keys).
+    Every buffer's out region must hold the full result."""
+    import ctypes
+
+    torch = torch_cuda
+    L = X.lib()
+    b, nl, ni, d = 2, 100, 700, 768
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+    offs = (ctypes.c_longlong * 4)()
+    total = L.xattn_peer_layout(b * nl, d, offs)
+    ptrs, keep = [], []
+
+    def view(base, off, shape):
+        return torch.as_tensor(X._DeviceArray(base + int(off) * 4, shape), device="cuda")
+
+    try:
+        for lo, hi in ((0, 300), (300, 300), (300, 700)):
+            ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
+            assert L.xattn_ipc_alloc(total, ctypes.byref(ptr), handle) == 0
+            ptrs.append(ptr.value)
+            kl, vl = k[:, lo:hi].contiguous(), v[:, lo:hi].contiguous()
+            keep.append((kl, vl))
+            po, pm, pl = view(ptr.value, offs[2], (b, nl, d)), view(ptr.value, offs[0], (b, nl)), \
+                view(ptr.value, offs[1], (b, nl))
+            assert L.xattn_fp32_partial(q.data_ptr(), kl.data_ptr(), vl.data_ptr(), po.data_ptr(),
+                                        pm.data_ptr(), pl.data_ptr(), b, nl, hi - lo, d, None) == 0
+        bases = (ctypes.c_void_p * 3)(*ptrs)
+        assert L.xattn_peer_merge(bases, 3, -1, b * nl, d, 1, None) == 0
+        torch.cuda.synchronize()
+        ref = ref_attention(torch, q, k, v)
+        outs = [view(p, offs[3], (b, nl, d)).clone() for p in ptrs]
+        for o in outs:
+            assert_close(torch, o, ref, TF32_TOL, "peer merge emulation")
+            assert torch.equal(o, outs[0])
+    finally:
+        torch.cuda.synchronize()
+        for p in ptrs:
+            L.xattn_ipc_free(p)
+    assert X.device_status() == 0
+
+
+def test_empty_key_ranges_in_partial_and_split_entries(X, torch_cuda):
+    """N_input = 0 through the partial entry (a rank with an empty key slice) and the
+    split-K entry: empty partials (-FLT_MAX, 0, 0) and a zero output, as upstream's empty
+    splits (kernel_splitk.cu:62-71); the bf16 entry zero-fills its output too."""
+    torch = torch_cuda
+    q = torch.randn(2, 40, 768, device="cuda")
+    k = torch.empty(2, 0, 768, device="cuda")
+    po, pm, pl = X.cross_attention_partial(q, k, k)
+    torch.cuda.synchronize()
+    assert bool((pm == -3.4028234663852886e38).all()) and bool((pl == 0).all()) and bool((po == 0).all())
+    out, po, pm, pl = X.cross_attention_splitk(q, k, k, 3)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0
+    assert bool((pm == -3.4028234663852886e38).all()) and bool((pl == 0).all())
+    qb = torch.randn(1, 16, 4 * 64, device="cuda").bfloat16()
+    kb = torch.empty(1, 0, 4 * 64, device="cuda").bfloat16()
+    ob = torch.full_like(qb, 7.0)
+    X.cross_attention_bf16_mha(qb, kb, kb, 4, out=ob)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(ob.float()).item() == 0
+    assert X.device_status() == 0
+
+
 # ----------------------------------------------------------------------- failure detection
 def test_bounded_wait_gives_up_cleanly(X, torch_cuda):
     torch = torch_cuda
