@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm3x_kernel(const __grid_consta
       }
       for (int i = 0; i < kStages; ++i) {  // no copy in flight at exit
         if (--s < 0) { s = kStages - 1; phase ^= 1u; }
-        mbar_wait(smem_u32(&empty[s]), phase, kTimeoutDrain, nullptr);
+        mbar_wait(smem_u32(&empty[s]), phase, kTimeoutDrain, abort);
       }
     }
   } else if (warp == 1) {
@@ -173,6 +173,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm3x_kernel(const __grid_consta
 
   tc_fence_before();
   __syncthreads();
+  if (abort_flag) {  // stable here: every give_up preceded the barrier
+    settle_after_give_up();
+    __syncthreads();
+  }
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }

@@ -512,7 +512,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (pid == 0) {
         for (int k = max(0, i - kStages); k < i; ++k)
           mbar_wait(smem_u32(&bars.full[k % kStages]), static_cast<uint32_t>(k / kStages) & 1u,
-                    kTimeoutDrain, nullptr);
+                    kTimeoutDrain, abort);
       }
     }
   } else if (warp == 1) {
@@ -589,7 +589,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         mma_commit(smem_u32(&bars.o_done));
       }
       mma_commit(smem_u32(&bars.drain));
-      mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, nullptr);
+      mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, abort);
     }
   } else {
     // ================================================================ softmax / epilogue
@@ -798,6 +798,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // the peer may still be writing into this CTA's exchange buffer
+  if (abort_flag) settle_after_give_up();  // stable here: every give_up preceded the barrier
+  cluster_sync();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }

@@ -376,11 +376,12 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         }
       }
       // Drain (producer 0): the pair MMA releases every stage it consumed; wait for the last
-      // use of every slot so no load into this CTA's shared memory is still in flight at exit.
+      // use of every slot so no load into this CTA's shared memory is still in flight at exit
+      // (after a give-up the settle at the end covers them).
       if (pid == 0) {
         for (int k = max(0, i - kStages); k < i; ++k)
           mbar_wait(smem_u32(&bars.empty[k % kStages]), static_cast<uint32_t>(k / kStages) & 1u,
-                    kTimeoutDrain, nullptr);
+                    kTimeoutDrain, abort);
       }
     }
   } else if (warp == 1) {
@@ -540,7 +541,7 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
         U = u_end;
       }
       mma_commit_pair_mc(smem_u32(&bars.drain), static_cast<uint16_t>(1u << rank));
-      mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, nullptr);
+      mbar_wait(smem_u32(&bars.drain), 0, kTimeoutDrain, abort);
     } else if (!is_leader && comp) {
       // ============================================================ truncation statistics
       // Warp 1 of the pair's second CTA issues nothing, so it measures the inputs' TF32
@@ -914,6 +915,8 @@ __global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) XATTN_TRACE_POINT(13, 0);
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no thread of the cluster issues anything after this
+  if (abort_flag) settle_after_give_up();  // stable here: every give_up preceded the barrier
   cluster_sync();
   tc_fence_after();
   if (warp == 0) tmem_dealloc_pair(tmem, kTmemCols);

@@ -248,9 +248,9 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
       // last Q) so no copy is in flight at exit
       for (int i = 0; i < n_stages; ++i) {
         if (--s < 0) { s = n_stages - 1; phase ^= 1u; }
-        mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, nullptr);
+        mbar_wait(smem_u32(&bars.empty[s]), phase, kTimeoutDrain, abort);
       }
-      if (it > 0) mbar_wait(smem_u32(&bars.q_full), (it - 1) & 1, kTimeoutDrain, nullptr);
+      if (it > 0) mbar_wait(smem_u32(&bars.q_full), (it - 1) & 1, kTimeoutDrain, abort);
     }
   } else if (warp == 1) {
     // ============================================================== MMA issuer
@@ -483,6 +483,10 @@ __global__ void __launch_bounds__(kThreads, 2) mha_bf16_kernel(const __grid_cons
 
   tc_fence_before();
   __syncthreads();
+  if (abort_flag) {  // stable here: every give_up preceded the barrier
+    settle_after_give_up();
+    __syncthreads();
+  }
   tc_fence_after();
   if (threadIdx.x == 0) XATTN_TRACE_POINT(13, 0);
   if (warp == 0) tmem_dealloc(tmem, kTmemCols);

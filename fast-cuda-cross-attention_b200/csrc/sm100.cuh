@@ -135,8 +135,42 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
   return ok != 0;
 }
 
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t n;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(n));
+  return n;
+}
+
+// A wait gave up: set the abort flag -- a __shared__ int at the same offset in every CTA of
+// the kernel -- in this CTA and in every other CTA of the cluster (1 CTA without clusters),
+// so that every role of every CTA stops waiting at its next poll instead of running into
+// its own bound.
+__device__ __forceinline__ void give_up(volatile int* abort) {
+  *abort = 1;
+  const uint32_t n = cluster_nctarank();
+  if (n > 1) {
+    const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(const_cast<int*>(abort)));
+    for (uint32_t r = 0; r < n; ++r) {
+      uint32_t ra;
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(r));
+      asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ra), "r"(1u) : "memory");
+    }
+  }
+}
+
+// After a give-up, at the kernel's end (after the last barrier that every thread of the
+// cluster passes once it stops issuing work): let copies, st.async stores, MMAs and
+// commits already aimed at this CTA's shared or tensor memory land before the CTA
+// releases them.  They complete within microseconds; 1 ms of global time is the margin.
+constexpr unsigned long long kSettleNs = 1000000ull;
+__device__ __forceinline__ void settle_after_give_up() {
+  const uint64_t t0 = global_ns();
+  while (global_ns() - t0 < kSettleNs) __nanosleep(1000);
+}
+
 // Bounded wait.  Returns false (and records `code`) if the phase did not complete
-// within XATTN_WAIT_NS, or immediately if *abort is already set by another role.
+// within XATTN_WAIT_NS, or immediately if *abort is already set by another role or CTA.
+// A wait that gives up sets the abort flag of every CTA of the cluster (give_up).
 template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code,
                                           volatile int* abort) {
@@ -149,7 +183,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
       if (abort != nullptr && *abort) return false;
       if (global_ns() - t0 > g_wait_ns) {
         record_status(code);
-        if (abort != nullptr) *abort = 1;
+        if (abort != nullptr) give_up(abort);
         return false;
       }
     }
@@ -183,7 +217,7 @@ __device__ __forceinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity, in
       if (abort != nullptr && *abort) return false;
       if (global_ns() - t0 > g_wait_ns) {
         record_status(code);
-        if (abort != nullptr) *abort = 1;
+        if (abort != nullptr) give_up(abort);
         return false;
       }
     }

@@ -1177,14 +1177,20 @@ extern "C" int xattn_trace_fetch(unsigned long long* host) {
 namespace xattn {
 namespace {
 
-constexpr size_t kNoAllocScratchFloats = static_cast<size_t>(8) << 20;  // 32 MiB of fp32
+// The documented limit, B * N_latent * num_splits * (dim + 2) floats (32 MiB), plus room for
+// the 256-byte alignment of the three sub-arrays (at most 3 * 63 floats), so that every
+// request within the documented limit fits.
+constexpr size_t kNoAllocLimitFloats = static_cast<size_t>(8) << 20;
+constexpr size_t kNoAllocScratchFloats = kNoAllocLimitFloats + 192;
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
+constexpr int kNoAllocDevices = 64;
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[64] = {};
+float* g_noalloc_ptr[kNoAllocDevices] = {};
 
 // Device address of the scratch array on device `dev` (current), looked up on first use.
 float* noalloc_scratch(int dev) {
+  if (dev < 0 || dev >= kNoAllocDevices) return nullptr;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* ptr = nullptr;
@@ -1213,7 +1219,7 @@ extern "C" int xattn_splitk_noalloc(const float* Q, const float* K, const float*
   // rows * num_splits * (dim + 2) <= capacity, tested by division so that no product can
   // wrap around (each factor is below 2^62 and 2^32)
   const size_t per_row = static_cast<size_t>(num_splits) * (static_cast<size_t>(dim) + 2);
-  if (per_row > kNoAllocScratchFloats / rows) return set_error(XATTN_ERR_TOO_LARGE);
+  if (per_row > kNoAllocLimitFloats / rows) return set_error(XATTN_ERR_TOO_LARGE);
   const size_t po_elems = round_up64(rows * num_splits * dim);
   const size_t ml_elems = round_up64(rows * num_splits);
   if (po_elems + 2 * ml_elems > kNoAllocScratchFloats) return set_error(XATTN_ERR_TOO_LARGE);
@@ -1226,9 +1232,13 @@ extern "C" int xattn_splitk_noalloc(const float* Q, const float* K, const float*
   float* pl = pm + ml_elems;
   const int chunk = std::max(1, (N_input + num_splits - 1) / num_splits);  // kernel_splitk.cu:59
   const float scale_log2 = kLog2e / std::sqrt(static_cast<float>(dim));
+  // the kernel choice of launch_splitk_kernel (run_splitk)
   if (g_opt_path.load() == 2 || !tc_fp32_supported(Q, K, V, output, dim))
     rc = launch_simt<float, float>(Q, K, V, nullptr, po, pm, pl, batch_size, 1, N_latent, N_input,
                                    dim, num_splits, chunk, 1, scale_log2, stream);
+  else if (g_opt_kernel.load() != 1 && pair4::supports_dh(dim / 2))
+    rc = launch_fused_pair<float>(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim,
+                                  num_splits, chunk, 1, stream);
   else
     rc = launch_fused(Q, K, V, nullptr, po, pm, pl, batch_size, N_latent, N_input, dim,
                       num_splits, chunk, 1, stream);

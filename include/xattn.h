@@ -142,10 +142,10 @@ int xattn_plan_fp32(int batch_size, int N_latent, int N_input, int dim, int* num
 
 /* Split-K attention that allocates nothing.  No counterpart in the upstream project.
  *
- * Same key-split rule, result and tolerance as launch_splitk_kernel, but the caller passes
- * only Q, K, V and the output: the (m, l, O) partials live in one scratch array compiled
- * into the library (32 MiB, held by every GPU that loads the library until the process
- * exits).  It is meant for callers that may not allocate device memory during a call:
+ * Same key-split rule, kernels, result and tolerance as launch_splitk_kernel, but the caller
+ * passes only Q, K, V and the output: the (m, l, O) partials live in one scratch array
+ * compiled into the library (32 MiB plus 768 bytes of alignment room, held by every GPU
+ * that loads the library until the process exits).  It is meant for callers that may not allocate device memory during a call:
  * programs that hand the whole GPU to their own memory pool at start-up, where an extra
  * cudaMalloc would fail or fragment that pool, and latency-critical loops that cannot
  * afford the device-wide synchronisation a cudaMalloc / cudaFree can cause.  (The

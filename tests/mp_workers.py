@@ -148,3 +148,41 @@ def nccl_split_worker(rank, world, port, results):
         results.put((rank, errs, status, None))
     except Exception:
         results.put((rank, None, None, traceback.format_exc()))
+
+
+def give_up_worker(kind, results):
+    """Child process of tests/test_give_up_gpu.py: one call of a tensor-core kernel with the
+    device wait bound set to 1 us, so that its waits give up mid-pipeline; then the bound
+    back at 2 s and the same call again.  Reports (status after the first call, error of the
+    second call relative to max|O_ref|, status after the second call)."""
+    import math
+
+    try:
+        import torch
+
+        import xattn
+
+        torch.cuda.set_device(0)
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        b, nl = {"pair": (8, 1024), "split": (1, 64), "two_cta": (2, 256)}[kind]
+        ni, d = 784, 768
+        q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
+        if kind == "two_cta":
+            xattn.set_option(xattn.OPT_KERNEL, 1)
+
+        def call():
+            return xattn.cross_attention(q, k, v)
+
+        ref = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(d), -1) @ v.double()
+        xattn.set_option(xattn.OPT_WAIT_US, 1)
+        try:
+            call()
+        finally:
+            st1 = xattn.device_status(clear=True)  # synchronises; -1 if the context were lost
+            xattn.set_option(xattn.OPT_WAIT_US, 2000000)
+        out = call()
+        torch.cuda.synchronize()
+        err = (out.double() - ref).abs().max().item() / ref.abs().max().item()
+        results.put((st1, err, xattn.device_status(clear=True), None))
+    except Exception:
+        results.put((None, None, None, traceback.format_exc()))

@@ -80,3 +80,31 @@ def test_noalloc_refuses_oversize_problem():
     assert lib.xattn_last_error() == XATTN_ERR_TOO_LARGE
     torch.cuda.synchronize()
     assert bool((out == 3.0).all())
+
+
+@pytest.mark.parametrize("shape,splits", [
+    ((1, 64, 10, 768), 8),    # 10 keys over 8 splits of 2: splits 5..7 are empty
+    ((2, 33, 70, 100), 3),    # D = 100: the CUDA-core kernel, not the tensor cores
+    ((1, 2048, 64, 510), 8),  # exactly the documented limit: 1 * 2048 * 8 * (510 + 2) = 8,388,608
+], ids=["empty-trailing-splits", "cuda-core-path", "at-the-limit"])
+def test_noalloc_edge_cases_match_existing_entry(shape, splits):
+    """The same comparison on the shapes where the shared scratch array is used differently:
+    empty trailing splits (their (-FLT_MAX, 0, 0) partials come from the kernel, not from a
+    cleared array), the CUDA-core path, and a request exactly at the size limit."""
+    import torch
+
+    import xattn
+
+    lib = xattn.lib()
+    q, k, v = _inputs(torch, *shape, 31)
+    ref, _, _, _ = xattn.cross_attention_splitk(q, k, v, splits)
+    out = torch.full_like(q, float("nan"))
+    assert _noalloc(lib, q, k, v, out, splits) == 0
+    torch.cuda.synchronize()
+    scale = ref.abs().max().item()
+    assert torch.isfinite(out).all()
+    assert (out - ref).abs().max().item() <= TF32_TOL * scale
+    exact = torch.softmax(q.double() @ k.double().transpose(1, 2) / math.sqrt(q.shape[-1]), -1) @ v.double()
+    assert (out.double() - exact).abs().max().item() <= TF32_TOL * scale
+    assert xattn.device_status() == 0
+
