@@ -159,12 +159,16 @@ __device__ __forceinline__ float trunc_ratio(float num, float den) {
 }
 
 // Truncation sums of one item of the four-CTA pair kernel, taken by one warp: one 16-byte
-// piece of each of the item's 256 query rows (rows past N_latent skipped), kept apart per
-// 128-row half, and 128 pieces each of K and V spread over the key range [k_begin, k_end)
-// -- 512 values of each.  s = {sum d x, sum x x} of rows 0..127, of rows 128..255, of K, of
-// V, identical in every lane (xor butterfly).  All sixteen loads are issued before any is
-// used (one memory round trip).  Positions depend on the item only, so the two pairs of a
-// cluster (the two halves of D) compute bit-identical sums.
+// piece of every fourth of the item's 256 query rows (rows past N_latent skipped), kept
+// apart per 128-row half, and 32 pieces each of K and V spread over the key range
+// [k_begin, k_end) -- 128 values of each, which pins e to a few percent of itself (the
+// compensation's own error is then ~1e-5 of a score).  The sample is deliberately small:
+// it reads ahead, into L2, lines of an item that has not started, and at the C3 shape
+// (inputs beyond L2) 16 pieces per lane instead of 4 cost ~2 % of the kernel's time.
+// s = {sum d x, sum x x} of rows 0..127, of rows 128..255, of K, of V, identical in every
+// lane (xor butterfly).  All four loads are issued before any is used.  Positions depend on
+// the item only, so the two pairs of a cluster (the two halves of D) compute bit-identical
+// sums.
 __device__ __forceinline__ int trunc_piece_col(unsigned key, unsigned c4) {
   return 4 * static_cast<int>(__umulhi(key * 0x9E3779B1u, c4));  // hashed 16-byte piece < c4
 }
@@ -173,31 +177,26 @@ __device__ __forceinline__ void trunc_warp_sample(const Params& p, int b, int ro
   const unsigned c4 = static_cast<unsigned>(p.dim / 4);  // 16-byte pieces per row
   const int nk = k_end - k_begin;
   const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 x[16];
+  float4 x[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {  // query rows row_base + lane + 32 i
-    const int row = row_base + lane + 32 * i;
+  for (int i = 0; i < 2; ++i) {  // query rows row_base + 128 i + 4 lane
+    const int row = row_base + kRows * i + 4 * lane;
     x[i] = row < p.n_latent
                ? __ldg(reinterpret_cast<const float4*>(p.q + (static_cast<size_t>(b) * p.n_latent + row) * p.dim +
                                                        trunc_piece_col(static_cast<unsigned>(row), c4)))
                : zero;
   }
+  const int key = k_begin + static_cast<int>((static_cast<long long>(lane) * nk) >> 5);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {  // K (i < 4) and V pieces 0..127
-    const unsigned piece = static_cast<unsigned>(lane + 32 * (i & 3));
-    const int key = k_begin + static_cast<int>((static_cast<long long>(piece) * nk) >> 7);
-    const float* src = i < 4 ? p.k : p.v;
-    x[8 + i] = nk > 0 ? __ldg(reinterpret_cast<const float4*>(src + (static_cast<size_t>(b) * p.n_input + key) * p.dim +
-                                                              trunc_piece_col(piece * 2u + (i < 4 ? 1u : 2u), c4)))
+  for (int i = 0; i < 2; ++i)  // K, V
+    x[2 + i] = nk > 0 ? __ldg(reinterpret_cast<const float4*>((i == 0 ? p.k : p.v) +
+                                                              (static_cast<size_t>(b) * p.n_input + key) * p.dim +
+                                                              trunc_piece_col(2u * lane + 1u + i, c4)))
                       : zero;
-  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) s[i] = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int t = i < 4 ? 0 : (i < 8 ? 1 : (i < 12 ? 2 : 3));  // rows 0..127, 128..255, K, V
-    trunc_add(x[i], s[2 * t], s[2 * t + 1]);
-  }
+  for (int i = 0; i < 4; ++i) trunc_add(x[i], s[2 * i], s[2 * i + 1]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
