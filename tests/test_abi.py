@@ -121,3 +121,30 @@ def test_upstream_wrapper_binds_this_library_unchanged(tmp_path):
     res = subprocess.run(["python", "-c", code], cwd=tmp_path, capture_output=True, text=True)
     assert res.returncode == 0, res.stderr
     assert "vectorized" in res.stdout
+
+
+def test_peer_exchange_layout_and_argument_checks():
+    """xattn_peer_layout: the four regions of a rank's exchange buffer start on 256-byte
+    boundaries, follow the flag words and do not overlap; xattn_peer_merge refuses bad
+    arguments before any device call (so this runs without a GPU)."""
+    lib = ctypes.CDLL(LIB)
+    lay = lib.xattn_peer_layout
+    lay.argtypes = [ctypes.c_longlong, ctypes.c_int, ctypes.POINTER(ctypes.c_longlong)]
+    lay.restype = ctypes.c_longlong
+    for rows, dim in ((4096, 768), (1, 64), (333, 100)):
+        off = (ctypes.c_longlong * 4)()
+        total = lay(rows, dim, off)
+        pm, pl, po, out = list(off)
+        assert all(o % 64 == 0 for o in off) and pm >= 64
+        assert pl >= pm + rows and po >= pl + rows and out >= po + rows * dim
+        assert total >= 4 * (out + rows * dim) and total % 256 == 0
+    assert lay(-1, 768, None) == -1
+    merge = lib.xattn_peer_merge
+    merge.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_int,
+                      ctypes.c_uint, ctypes.c_void_p]
+    merge.restype = ctypes.c_int
+    bases = (ctypes.c_void_p * 9)(*([256] * 9))
+    assert merge(None, 2, 0, 10, 768, 1, None) == 1          # no buffers
+    assert merge(bases, 9, 0, 10, 768, 1, None) == 1         # more than eight ranks
+    assert merge(bases, 2, 2, 10, 768, 1, None) == 1         # rank out of range
+    assert merge(bases, 2, 0, 10, 0, 1, None) == 1           # no columns
