@@ -94,8 +94,12 @@ stop = []
 signal.signal(signal.SIGINT, lambda *a: stop.append(1))  # only a flag: no write is cut short
 pynvml.nvmlInit()
 h = pynvml.nvmlDeviceGetHandleByPciBusId(sys.argv[1])
-print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
 out = []
+# one sample before the "max" line the parent waits for, so that the first (slow) queries
+# are over before its timed region starts
+pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+print("max", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
 while not stop:
     sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
     r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)

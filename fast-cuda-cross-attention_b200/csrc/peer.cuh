@@ -102,6 +102,9 @@ __global__ void __launch_bounds__(kThreads) merge_kernel(const Params a) {
   __shared__ float* base[kMaxRanks];  // a.base, indexed at run time without a local copy
   __shared__ int go;
   const bool emulate = a.rank < 0;
+  // launched as a programmatic dependent of the kernel that writes this rank's partials:
+  // nothing below touches memory before that kernel has completed
+  griddep_wait();
   if (threadIdx.x == 0) {
 #pragma unroll
     for (int i = 0; i < kMaxRanks; ++i) base[i] = a.base[i];

@@ -107,15 +107,17 @@ __global__ void __launch_bounds__(kWarps * 32) attention_kernel(const Args<Tin, 
 }
 
 // Log-sum-exp merge of S split partials per row (upstream kernel_splitk.cu:186-236):
-// M = max_s m_s; L = sum_s e^(m_s-M) l_s; O = sum_s e^(m_s-M) O_s / L.  Splits whose
-// m is -FLT_MAX (empty) are skipped.  Block (row, column slice) of kCombineThreads threads:
-// warp 0 reduces the row's split weights w_s = e^(m_s-M) / L into shared memory once, then
-// each thread merges four columns at a time with independent loads across the splits.
-// Dynamic shared memory: num_splits floats.  kPartial: write the merged partial instead of
-// the normalised output -- O_u = sum_s e^(m_s-M) O_s (unnormalised) to out, M to pm_out and
-// L to pl_out (a row with no keys keeps the empty-split triple -FLT_MAX, 0, 0).
-constexpr int kCombineThreads = 128;
-constexpr int kCombineCols = 4 * kCombineThreads;  // columns per block (float4 per thread)
+// M = max_s m_s; L = sum_s e^(m_s-M) l_s; O = sum_s e^(m_s-M) O_s / L.  Splits whose m is
+// -FLT_MAX (empty) get weight 0.  One thread per (row, four columns): the partial outputs do
+// not depend on the weights, so the thread issues its loads of up to kCombineChunk splits'
+// outputs together with their (m, l) and only then forms the weights -- one memory round trip
+// per chunk of splits, merged across chunks with a running maximum (online log-sum-exp).  No
+// shared memory, no block barrier.  kPartial: write the merged partial instead of the
+// normalised output -- O_u = sum_s e^(m_s-M) O_s (unnormalised) to out, M to pm_out and L to
+// pl_out (a row with no keys keeps the empty-split triple -FLT_MAX, 0, 0).
+// po rows: [rows][S][dim] (the upstream layout).
+constexpr int kCombineThreads = 256;
+constexpr int kCombineChunk = 4;
 
 template <typename Tout, bool kPartial = false>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* __restrict__ po,
@@ -126,66 +128,71 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(const float* _
                                                                   int num_splits, int ld_o,
                                                                   float* __restrict__ pm_out = nullptr,
                                                                   float* __restrict__ pl_out = nullptr) {
-  extern __shared__ float w[];
+  // a dependent launched with programmatic serialization (the multi-GPU merge) may take free
+  // SM slots now; it waits in griddep_wait() for this grid's results
+  griddep_launch_dependents();
   griddep_wait();  // launched as a programmatic dependent of the kernel writing the partials
-  const long long r = blockIdx.x;
-  if (r >= rows) return;
-  const float* m = pm + r * num_splits;
-  const float* l = pl + r * num_splits;
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    float mx = -INFINITY;
-    for (int s = lane; s < num_splits; s += 32)
-      if (m[s] > -3.4028234663852886e38f) mx = fmaxf(mx, m[s]);
+  constexpr float kEmpty = -3.4028234663852886e38f;
+  const int S = num_splits;
+  // float4 loads need 16-byte aligned rows: dim % 4 == 0 and an aligned po (caller scratch of
+  // the upstream split entry may be any float pointer); otherwise one column per thread
+  const bool vec = (dim & 3) == 0 && (reinterpret_cast<uintptr_t>(po) & 15) == 0;
+  const int w = vec ? 4 : 1;              // columns per thread
+  const int per_row = (dim + w - 1) / w;  // threads per row
+  const long long idx = static_cast<long long>(blockIdx.x) * kCombineThreads + threadIdx.x;
+  if (idx >= rows * per_row) return;
+  const long long r = idx / per_row;
+  const int c = static_cast<int>(idx - r * per_row) * w;
+  const float* src = po + r * S * static_cast<long long>(dim) + c;
+  const float* m = pm + r * S;
+  const float* l = pl + r * S;
+  float mx = -INFINITY, lsum = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < S; s0 += kCombineChunk) {
+    float4 x[kCombineChunk];
+    float ms[kCombineChunk], ls[kCombineChunk];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float lsum = 0.f;
-    for (int s = lane; s < num_splits; s += 32) {
-      const float e = m[s] > -3.4028234663852886e38f ? __expf(m[s] - mx) : 0.f;
-      w[s] = e;
-      lsum += e * l[s];
+    for (int j = 0; j < kCombineChunk; ++j) {
+      const bool in = s0 + j < S;
+      const float* row = src + static_cast<long long>(s0 + j) * dim;
+      if (vec)
+        x[j] = in ? *reinterpret_cast<const float4*>(row) : make_float4(0.f, 0.f, 0.f, 0.f);
+      else
+        x[j] = make_float4(in ? row[0] : 0.f, 0.f, 0.f, 0.f);
+      ms[j] = in ? m[s0 + j] : kEmpty;
+      ls[j] = in ? l[s0 + j] : 0.f;
     }
+    float cm = mx;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    const float inv = kPartial ? 1.f : (lsum > 0.f ? 1.f / lsum : 0.f);  // no keys: zeros
-    if (kPartial && lane == 0 && blockIdx.y == 0) {
-      pm_out[r] = lsum > 0.f ? mx : -3.4028234663852886e38f;
-      pl_out[r] = lsum;
+    for (int j = 0; j < kCombineChunk; ++j)
+      if (ms[j] > kEmpty) cm = fmaxf(cm, ms[j]);
+    if (cm == -INFINITY) continue;  // nothing but empty splits so far
+    const float f = __expf(mx - cm);  // 0 while mx is still -inf
+    lsum *= f;
+    acc.x *= f;
+    acc.y *= f;
+    acc.z *= f;
+    acc.w *= f;
+#pragma unroll
+    for (int j = 0; j < kCombineChunk; ++j) {
+      const float e = ms[j] > kEmpty ? __expf(ms[j] - cm) : 0.f;
+      lsum = fmaf(e, ls[j], lsum);
+      acc.x = fmaf(e, x[j].x, acc.x);
+      acc.y = fmaf(e, x[j].y, acc.y);
+      acc.z = fmaf(e, x[j].z, acc.z);
+      acc.w = fmaf(e, x[j].w, acc.w);
     }
-    __syncwarp();
-    for (int s = lane; s < num_splits; s += 32) w[s] *= inv;
+    mx = cm;
   }
-  __syncthreads();
-  const float* src = po + r * num_splits * static_cast<long long>(dim);
-  Tout* dst = out + r * static_cast<long long>(ld_o);
-  const int c0 = blockIdx.y * kCombineCols + 4 * threadIdx.x;
-  // float4 loads need a 16-byte aligned row start: dim % 4 == 0 and an aligned po (caller
-  // scratch of the upstream split entry may be any float pointer)
-  if ((dim & 3) == 0 && (reinterpret_cast<uintptr_t>(po) & 15) == 0) {
-    if (c0 >= dim) return;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int s = 0; s < num_splits; ++s) {
-      const float ws = w[s];
-      if (ws == 0.f) continue;
-      const float4 x = *reinterpret_cast<const float4*>(src + static_cast<long long>(s) * dim + c0);
-      acc.x = fmaf(ws, x.x, acc.x);
-      acc.y = fmaf(ws, x.y, acc.y);
-      acc.z = fmaf(ws, x.z, acc.z);
-      acc.w = fmaf(ws, x.w, acc.w);
-    }
-    from_f(&dst[c0], acc.x);
-    from_f(&dst[c0 + 1], acc.y);
-    from_f(&dst[c0 + 2], acc.z);
-    from_f(&dst[c0 + 3], acc.w);
-  } else {
-    for (int c = c0; c < min(c0 + 4, dim); ++c) {
-      float acc = 0.f;
-      for (int s = 0; s < num_splits; ++s)
-        if (w[s] != 0.f) acc = fmaf(w[s], src[static_cast<long long>(s) * dim + c], acc);
-      from_f(&dst[c], acc);
-    }
+  const float inv = kPartial ? 1.f : (lsum > 0.f ? 1.f / lsum : 0.f);  // no keys: zeros
+  if (kPartial && c == 0) {
+    pm_out[r] = lsum > 0.f ? mx : kEmpty;
+    pl_out[r] = lsum;
   }
+  Tout* dst = out + r * static_cast<long long>(ld_o) + c;
+  const float v[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+  for (int e = 0; e < w; ++e)
+    if (c + e < dim) from_f(&dst[e], v[e]);
 }
 
 // Multi-GPU N_input split, step 2: after an all-reduce MAX of the row maxima into

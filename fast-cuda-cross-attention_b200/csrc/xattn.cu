@@ -435,21 +435,19 @@ int launch_combine(const float* po, const float* pm, const float* pl, float* out
                    float* pl_out = nullptr) {
   if (rows <= 0) return XATTN_OK;
   if (rows > 0x7fffffffLL || num_splits <= 0) return XATTN_ERR_ARG;
-  const size_t smem = static_cast<size_t>(num_splits) * sizeof(float);
-  if (smem > 227 * 1024) return XATTN_ERR_ARG;
   auto kern = pm_out != nullptr ? simt::combine_kernel<float, true> : simt::combine_kernel<float, false>;
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(smem)) != cudaSuccess)
-    return XATTN_ERR_LAUNCH;
+  const bool vec = (D & 3) == 0 && (reinterpret_cast<uintptr_t>(po) & 15) == 0;  // as the kernel
+  const long long threads = rows * (vec ? (D + 3) / 4 : D);
+  const long long blocks = (threads + simt::kCombineThreads - 1) / simt::kCombineThreads;
+  if (blocks > 0x7fffffffLL) return XATTN_ERR_ARG;
   // Programmatic stream serialization: the combine's CTAs may launch while the partial
   // kernel still runs (the pair kernel triggers at its start) and wait in griddep_wait()
   // for its results, so the kernel boundary costs no launch latency.  After any other
   // stream operation this is ordinary stream order.
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(rows), (D + simt::kCombineCols - 1) / simt::kCombineCols);
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks));
   cfg.blockDim = dim3(simt::kCombineThreads);
-  cfg.dynamicSmemBytes = smem;
+  cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1158,8 +1156,18 @@ extern "C" int xattn_peer_merge(void* const* bases, int n_ranks, int rank, long 
   // a warp per row; at least one block, so that every rank takes part in both barriers
   const long long want = (mine + peer::kThreads / 32 - 1) / (peer::kThreads / 32);
   const unsigned blocks = static_cast<unsigned>(std::max<long long>(1, std::min<long long>(want, sm_count(dev) * 4LL)));
-  peer::merge_kernel<<<blocks, peer::kThreads, 0, stream>>>(a);
-  return set_error(cudaPeekAtLastError() == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
+  // programmatic stream serialization: the launch and the blocks' start overlap the
+  // partial's last kernel, which triggers its dependents early
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(peer::kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return set_error(cudaLaunchKernelEx(&cfg, peer::merge_kernel, a) == cudaSuccess ? XATTN_OK : XATTN_ERR_LAUNCH);
 }
 
 #ifdef XATTN_TRACE
