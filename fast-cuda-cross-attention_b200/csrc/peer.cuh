@@ -34,7 +34,7 @@ namespace xattn {
 namespace peer {
 
 constexpr int kMaxRanks = 8;
-constexpr int kThreads = 256;  // eight warps, one row each at a time
+constexpr int kThreads = 256;  // eight warps, one (row, column segment) each at a time
 constexpr int kReadySlot = 0, kDoneSlot = 32, kCounterSlot = 63, kFlagWords = 64;
 
 struct Layout {
@@ -70,14 +70,25 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
+// base[i] for a run-time i without indexing the parameter array at run time (which would
+// copy it to local memory)
+__device__ __forceinline__ float* pick(float* const (&base)[kMaxRanks], int i) {
+  float* r = base[0];
+#pragma unroll
+  for (int p = 1; p < kMaxRanks; ++p)
+    if (i == p) r = base[p];
+  return r;
+}
+
 // Barrier among the ranks on the flags at `slot`: announce the epoch to every rank, wait
-// for every rank's announcement.  Called by one thread; `base` is the block's shared copy
-// of the buffers' addresses.
-__device__ __forceinline__ bool rank_barrier(float* const* base, int n_ranks, int rank, unsigned epoch,
-                                             int slot) {
+// for every rank's announcement.  Called by one thread.
+__device__ __forceinline__ bool rank_barrier(float* const (&base)[kMaxRanks], int n_ranks, int rank,
+                                             unsigned epoch, int slot) {
   __threadfence_system();
-  for (int p = 0; p < n_ranks; ++p) st_release_sys(reinterpret_cast<unsigned*>(base[p]) + slot + rank, epoch);
-  const unsigned* f = reinterpret_cast<const unsigned*>(base[rank]) + slot;
+#pragma unroll
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (p < n_ranks) st_release_sys(reinterpret_cast<unsigned*>(base[p]) + slot + rank, epoch);
+  const unsigned* f = reinterpret_cast<const unsigned*>(pick(base, rank)) + slot;
   const uint64_t t0 = global_ns();
   for (int p = 0; p < n_ranks; ++p) {
     while (static_cast<int>(ld_acquire_sys(f + p) - epoch) < 0) {
@@ -91,96 +102,112 @@ __device__ __forceinline__ bool rank_barrier(float* const* base, int n_ranks, in
   return true;
 }
 
-// One warp per row (grid-stride over this rank's rows): lanes < n load the ranks' (m, l),
-// the weights w_p = e^(m_p - M) / L come out of two shuffle reductions, then for each rank
-// every lane issues its loads of that rank's row (kVec float4 per lane per pass) before
-// using any, so a row costs one remote round trip per rank, and the warps of all resident
-// blocks keep the whole slice in flight.
-constexpr int kVec = 8;  // float4 per lane per pass: 1024 columns
+// One warp per unit = (row, segment of kSegCols columns), grid-stride over this rank's rows:
+// lanes < n load the ranks' (m, l) while every lane issues its loads of the segment from ALL
+// ranks (kSegVec float4 per lane per rank, the rank loop unrolled to kMaxRanks), so a unit
+// costs one remote round trip whatever the rank count; the weights w_p = e^(m_p - M) / L come
+// out of two shuffle reductions, and the merged segment is stored into every rank's out.
+constexpr int kSegVec = 2;                  // float4 per lane per rank
+constexpr int kSegCols = 32 * 4 * kSegVec;  // 256 columns per unit
+
+__device__ __forceinline__ float4 fma4(float w, float4 x, float4 acc) {
+  acc.x = fmaf(w, x.x, acc.x);
+  acc.y = fmaf(w, x.y, acc.y);
+  acc.z = fmaf(w, x.z, acc.z);
+  acc.w = fmaf(w, x.w, acc.w);
+  return acc;
+}
 
 __global__ void __launch_bounds__(kThreads) merge_kernel(const Params a) {
-  __shared__ float* base[kMaxRanks];  // a.base, indexed at run time without a local copy
   __shared__ int go;
   const bool emulate = a.rank < 0;
   // launched as a programmatic dependent of the kernel that writes this rank's partials:
   // nothing below touches memory before that kernel has completed
   griddep_wait();
-  if (threadIdx.x == 0) {
-#pragma unroll
-    for (int i = 0; i < kMaxRanks; ++i) base[i] = a.base[i];
-    go = emulate ? 1 : rank_barrier(base, a.n_ranks, a.rank, a.epoch, kReadySlot);
-  }
+  if (threadIdx.x == 0) go = emulate ? 1 : rank_barrier(a.base, a.n_ranks, a.rank, a.epoch, kReadySlot);
   __syncthreads();
   const int n = a.n_ranks, lane = threadIdx.x % 32;
   const long long r0 = emulate ? 0 : a.rows * a.rank / n;
   const long long r1 = emulate ? a.rows : a.rows * (a.rank + 1) / n;
-  const long long wpb = kThreads / 32;
   const bool vec = (a.dim & 3) == 0;
-  for (long long r = r0 + blockIdx.x * wpb + threadIdx.x / 32; go && r < r1; r += gridDim.x * wpb) {
+  const int nseg = vec ? (a.dim + kSegCols - 1) / kSegCols : (a.dim + 31) / 32;
+  const long long units = (r1 - r0) * nseg;
+  const long long wpb = kThreads / 32;
+  for (long long u = blockIdx.x * wpb + threadIdx.x / 32; go && u < units; u += gridDim.x * wpb) {
+    const long long r = r0 + u / nseg;
+    const int seg = static_cast<int>(u % nseg);
+    const long long off = r * a.dim;
     float m = -INFINITY, l = 0.f;
     if (lane < n) {
-      m = __ldcg(base[lane] + a.lay.pm + r);
-      l = __ldcg(base[lane] + a.lay.pl + r);
-      if (!(m > -3.4028234663852886e38f)) m = -INFINITY;  // a rank without keys
+      const float* bl = pick(a.base, lane);
+      m = __ldcg(bl + a.lay.pm + r);
+      l = __ldcg(bl + a.lay.pl + r);
     }
-    float mx = m;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float e = m > -INFINITY ? __expf(m - mx) : 0.f;
-    float lsum = e * l;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
-    const float w = lsum > 0.f ? e / lsum : 0.f;  // no keys anywhere: zeros
-    const long long off = r * a.dim;
     if (vec) {
-      for (int c0 = 0; c0 < a.dim; c0 += 32 * 4 * kVec) {
-        float4 acc[kVec];
+      float4 x[kMaxRanks][kSegVec];
 #pragma unroll
-        for (int j = 0; j < kVec; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int p = 0; p < n; ++p) {
-          const float wp = __shfl_sync(0xffffffffu, w, p);
-          if (wp == 0.f) continue;  // warp-uniform
-          float4 x[kVec];
+      for (int p = 0; p < kMaxRanks; ++p)
 #pragma unroll
-          for (int j = 0; j < kVec; ++j) {
-            const int c = c0 + 4 * (lane + 32 * j);
-            x[j] = c < a.dim ? __ldcg(reinterpret_cast<const float4*>(base[p] + a.lay.po + off + c))
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-#pragma unroll
-          for (int j = 0; j < kVec; ++j) {
-            acc[j].x = fmaf(wp, x[j].x, acc[j].x);
-            acc[j].y = fmaf(wp, x[j].y, acc[j].y);
-            acc[j].z = fmaf(wp, x[j].z, acc[j].z);
-            acc[j].w = fmaf(wp, x[j].w, acc[j].w);
-          }
+        for (int j = 0; j < kSegVec; ++j) {
+          const int c = seg * kSegCols + 4 * (lane + 32 * j);
+          x[p][j] = p < n && c < a.dim ? __ldcg(reinterpret_cast<const float4*>(a.base[p] + a.lay.po + off + c))
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        for (int p = 0; p < n; ++p)
+      if (!(m > -3.4028234663852886e38f)) m = -INFINITY;  // a rank without keys
+      float mx = m;
 #pragma unroll
-          for (int j = 0; j < kVec; ++j) {
-            const int c = c0 + 4 * (lane + 32 * j);
-            if (c < a.dim) *reinterpret_cast<float4*>(base[p] + a.lay.out + off + c) = acc[j];
-          }
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float e = m > -INFINITY ? __expf(m - mx) : 0.f;
+      float lsum = e * l;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+      const float w = lsum > 0.f ? e / lsum : 0.f;  // no keys anywhere: zeros
+      float4 acc[kSegVec];
+#pragma unroll
+      for (int j = 0; j < kSegVec; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) {
+        const float wp = __shfl_sync(0xffffffffu, w, p);  // 0 for p >= n
+#pragma unroll
+        for (int j = 0; j < kSegVec; ++j) acc[j] = fma4(wp, x[p][j], acc[j]);
       }
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+#pragma unroll
+        for (int j = 0; j < kSegVec; ++j) {
+          const int c = seg * kSegCols + 4 * (lane + 32 * j);
+          if (p < n && c < a.dim) *reinterpret_cast<float4*>(a.base[p] + a.lay.out + off + c) = acc[j];
+        }
     } else {
-      for (int c = lane; c < a.dim; c += 32) {
-        float acc = 0.f;
-        for (int p = 0; p < n; ++p) {
-          const float wp = __shfl_sync(0xffffffffu, w, p);
-          if (wp != 0.f) acc = fmaf(wp, __ldcg(base[p] + a.lay.po + off + c), acc);
-        }
-        for (int p = 0; p < n; ++p) base[p][a.lay.out + off + c] = acc;
-      }
+      const int c = seg * 32 + lane;
+      float x[kMaxRanks];
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) x[p] = p < n && c < a.dim ? __ldcg(a.base[p] + a.lay.po + off + c) : 0.f;
+      if (!(m > -3.4028234663852886e38f)) m = -INFINITY;
+      float mx = m;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float e = m > -INFINITY ? __expf(m - mx) : 0.f;
+      float lsum = e * l;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+      const float w = lsum > 0.f ? e / lsum : 0.f;
+      float acc = 0.f;
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) acc = fmaf(__shfl_sync(0xffffffffu, w, p), x[p], acc);
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p)
+        if (p < n && c < a.dim) a.base[p][a.lay.out + off + c] = acc;
     }
   }
   if (emulate) return;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence_system();  // this block's rows are visible in every rank's buffer
-    unsigned* counter = reinterpret_cast<unsigned*>(base[a.rank]) + kCounterSlot;
+    unsigned* counter = reinterpret_cast<unsigned*>(pick(a.base, a.rank)) + kCounterSlot;
     if (atomicAdd(counter, 1u) == gridDim.x - 1) {  // the last block of this launch
       *reinterpret_cast<volatile unsigned*>(counter) = 0u;  // for the next launch
-      rank_barrier(base, a.n_ranks, a.rank, a.epoch, kDoneSlot);
+      rank_barrier(a.base, a.n_ranks, a.rank, a.epoch, kDoneSlot);
     }
   }
 }

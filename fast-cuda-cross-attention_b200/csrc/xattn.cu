@@ -1153,9 +1153,11 @@ extern "C" int xattn_peer_merge(void* const* bases, int n_ranks, int rank, long 
   a.epoch = epoch;
   a.lay = peer::layout(rows, dim);
   const long long mine = rank < 0 ? rows : rows * (rank + 1) / n_ranks - rows * rank / n_ranks;
-  // a warp per row; at least one block, so that every rank takes part in both barriers
-  const long long want = (mine + peer::kThreads / 32 - 1) / (peer::kThreads / 32);
-  const unsigned blocks = static_cast<unsigned>(std::max<long long>(1, std::min<long long>(want, sm_count(dev) * 4LL)));
+  // a warp per (row, column segment), one wave of blocks (two per SM at the kernel's register
+  // count); at least one block, so that every rank takes part in both barriers
+  const long long nseg = (dim & 3) == 0 ? (dim + peer::kSegCols - 1) / peer::kSegCols : (dim + 31) / 32;
+  const long long want = (mine * nseg + peer::kThreads / 32 - 1) / (peer::kThreads / 32);
+  const unsigned blocks = static_cast<unsigned>(std::max<long long>(1, std::min<long long>(want, sm_count(dev) * 2LL)));
   // programmatic stream serialization: the launch and the blocks' start overlap the
   // partial's last kernel, which triggers its dependents early
   cudaLaunchConfig_t cfg = {};
