@@ -182,6 +182,16 @@ def _copy_streams(dev):
     return _COPY_STREAMS[dev.index]
 
 
+HOST_CHUNKS = 2  # default number of batch chunks of cross_attention_from_host
+
+
+def host_chunks(b: int, chunk: Optional[int] = None):
+    """Batch ranges [(c0, c1), ...] of cross_attention_from_host: chunks of `chunk` batches
+    (default ceil(b / HOST_CHUNKS))."""
+    c = max(1, chunk or (b + HOST_CHUNKS - 1) // HOST_CHUNKS)
+    return [(c0, min(b, c0 + c)) for c0 in range(0, b, c)]
+
+
 def cross_attention_from_host(q, k, v, out=None, chunk: Optional[int] = None):
     """cross_attention for host-resident fp32 q [B,Nl,D], k, v [B,Ni,D]; returns a host tensor.
 
@@ -189,13 +199,16 @@ def cross_attention_from_host(q, k, v, out=None, chunk: Optional[int] = None):
     chunk c+1 and the device->host copy of chunk c-1 run while chunk c computes, on the
     caller's current stream.  The two copy directions use separate copy engines, so a step
     costs about its host->device transfer instead of the sum of both transfers and the
-    kernels.  Device buffers persist per device for the last shape used (the output buffer
-    alternates between calls), so the next call's copy-in waits only for this call's last
-    kernel, not for its copy-out.  Inputs should be in pinned memory (otherwise the copies
-    are synchronous and nothing overlaps) and must not change until the caller's stream has
-    passed the call; `out` (host, pinned if given) receives the result.  The call returns
-    once the work is queued, with the caller's stream ordered after the last copy-out.
-    chunk: batches per chunk (default: the batch in 8 chunks).
+    kernels.  Device buffers persist per device for the last shape used, two sets of each
+    that alternate between calls: a call's copy-in waits only for the kernels of the call
+    before the previous one, so copy-ins of consecutive calls follow each other without a
+    gap, and a call's copy-out overlaps the next call's copy-in.  Every host->device copy
+    has a fixed cost (~20 us measured on B200 over PCIe), so the default is a few large
+    chunks.  Inputs should be in pinned memory (otherwise the copies are synchronous and
+    nothing overlaps) and must not change until the caller's stream has passed the call;
+    `out` (host, pinned if given) receives the result.  The call returns once the work is
+    queued, with the caller's stream ordered after the last copy-out.
+    chunk: batches per chunk (default: the batch in HOST_CHUNKS chunks).
     """
     import torch
 
@@ -209,28 +222,30 @@ def cross_attention_from_host(q, k, v, out=None, chunk: Optional[int] = None):
     s_in, s_out = _copy_streams(dev)
     if out is None:
         out = torch.empty(q.shape, dtype=torch.float32, pin_memory=True)
-    chunk = max(1, chunk or (b + 7) // 8)
     key = (tuple(q.shape), tuple(k.shape))
     st = _HOST_BUFFERS.get(dev.index)
     if st is None or st["key"] != key:
         if st is not None:  # the old buffers are idle before they go back to the allocator
             main.wait_stream(s_in)
             main.wait_stream(s_out)
-        st = {"key": key, "dq": torch.empty(q.shape, device=dev), "dk": torch.empty(k.shape, device=dev),
-              "dv": torch.empty(v.shape, device=dev),
-              "do": [torch.empty(q.shape, device=dev), torch.empty(q.shape, device=dev)],
-              "flip": 0, "computed": None}
+
+        def one_set():
+            return {"q": torch.empty(q.shape, device=dev), "k": torch.empty(k.shape, device=dev),
+                    "v": torch.empty(v.shape, device=dev), "o": torch.empty(q.shape, device=dev),
+                    "computed": None}
+
+        st = {"key": key, "sets": [one_set(), one_set()], "flip": 0}
         _HOST_BUFFERS[dev.index] = st
         s_in.wait_stream(main)   # buffers allocated on the caller's stream
         s_out.wait_stream(main)
-    dq, dk, dv = st["dq"], st["dk"], st["dv"]
-    do = st["do"][st["flip"]]  # the other one may still be copied out by the previous call
+    bs = st["sets"][st["flip"]]  # the other set may still be in use by the previous call
     st["flip"] ^= 1
-    if st["computed"] is not None:
-        s_in.wait_event(st["computed"])  # the previous call's kernels read dq, dk, dv
+    dq, dk, dv, do = bs["q"], bs["k"], bs["v"], bs["o"]
+    if bs["computed"] is not None:
+        s_in.wait_event(bs["computed"])  # the kernels of the call before the previous one
     done = None
-    for c0 in range(0, b, chunk):
-        sl = slice(c0, min(b, c0 + chunk))
+    for c0, c1 in host_chunks(b, chunk):
+        sl = slice(c0, c1)
         with torch.cuda.stream(s_in):
             dq[sl].copy_(q[sl], non_blocking=True)
             dk[sl].copy_(k[sl], non_blocking=True)
@@ -244,7 +259,7 @@ def cross_attention_from_host(q, k, v, out=None, chunk: Optional[int] = None):
         s_out.wait_event(done)
         with torch.cuda.stream(s_out):
             out[sl].copy_(do[sl], non_blocking=True)
-    st["computed"] = done
+    bs["computed"] = done
     main.wait_stream(s_out)
     return out
 
