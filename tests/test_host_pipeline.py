@@ -17,6 +17,24 @@ def test_host_entry_rejects_device_or_non_fp32_inputs():
         xattn.cross_attention_from_host(x, x, x)
 
 
+def test_host_chunks_cover_the_batch_once():
+    """The batch ranges of the host entry tile [0, B) in order without gaps or overlaps; the
+    default is HOST_CHUNKS chunks (fewer, larger copies: each host->device copy has a fixed
+    cost), an explicit chunk size gives equal chunks."""
+    import xattn
+
+    for b in (1, 2, 3, 7, 8, 31, 32, 33):
+        for chunk in (None, 1, 3, 40):
+            r = xattn.host_chunks(b, chunk)
+            assert r[0][0] == 0 and r[-1][1] == b
+            assert all(c1 > c0 for c0, c1 in r)
+            assert all(r[i][1] == r[i + 1][0] for i in range(len(r) - 1))
+            if chunk:
+                assert all(c1 - c0 == min(chunk, b - c0) for c0, c1 in r)
+            else:
+                assert len(r) == min(b, xattn.HOST_CHUNKS)
+
+
 def _ref(torch, q, k, v):
     q, k, v = q.double(), k.double(), v.double()
     return torch.softmax(q @ k.transpose(-1, -2) / math.sqrt(q.shape[-1]), -1) @ v
