@@ -633,17 +633,25 @@ def test_input_split_merge_kernels_single_gpu(X, torch_cuda):
     assert_close(torch, out, ref_attention(torch, q, k, v), TF32_TOL, "merge")
 
 
-def test_peer_merge_kernel_single_gpu_emulation(X, torch_cuda):
-    """xattn_peer_merge with rank = -1: one launch merges every row of three exchange
-    buffers of this GPU without the barriers -- the arithmetic and buffer layout of the
-    multi-GPU N_input split's one-kernel merge, on a ragged split with an empty key slice
-    (its partial is the (-FLT_MAX, 0, 0) triple xattn_fp32_partial writes for no keys).
-    Every buffer's out region must hold the full result."""
+# key-slice boundaries of the emulated ranks (one, three and eight ranks, each with a ragged
+# split; three and eight include an empty slice)
+PEER_SPLITS = [(0, 700), (0, 300, 300, 700), (0, 50, 50, 200, 330, 400, 520, 610, 700)]
+
+
+@pytest.mark.parametrize("bounds", PEER_SPLITS, ids=["1rank", "3ranks", "8ranks"])
+@pytest.mark.parametrize("d", [768, 98], ids=["D768", "D98"])
+def test_peer_merge_kernel_single_gpu_emulation(X, torch_cuda, bounds, d):
+    """xattn_peer_merge with rank = -1: one launch merges every row of the exchange buffers
+    of this GPU without the barriers -- the arithmetic and buffer layout of the multi-GPU
+    N_input split's one-kernel merge, on ragged splits with an empty key slice (its partial
+    is the (-FLT_MAX, 0, 0) triple xattn_fp32_partial writes for no keys), up to the eight
+    ranks the kernel's loads are unrolled for, with whole 256-column segments (D = 768) and
+    one column per lane (D = 98).  Every buffer's out region must hold the full result."""
     import ctypes
 
     torch = torch_cuda
     L = X.lib()
-    b, nl, ni, d = 2, 100, 700, 768
+    b, nl, ni = 2, 100, 700
     gen = torch.Generator(device="cuda").manual_seed(8)
     q, k, v = (torch.randn(b, n, d, device="cuda", generator=gen) for n in (nl, ni, ni))
     offs = (ctypes.c_longlong * 4)()
@@ -654,7 +662,7 @@ def test_peer_merge_kernel_single_gpu_emulation(X, torch_cuda):
         return torch.as_tensor(X._DeviceArray(base + int(off) * 4, shape), device="cuda")
 
     try:
-        for lo, hi in ((0, 300), (300, 300), (300, 700)):
+        for lo, hi in zip(bounds[:-1], bounds[1:]):
             ptr, handle = ctypes.c_void_p(), ctypes.create_string_buffer(64)
             assert L.xattn_ipc_alloc(total, ctypes.byref(ptr), handle) == 0
             ptrs.append(ptr.value)
@@ -664,8 +672,8 @@ def test_peer_merge_kernel_single_gpu_emulation(X, torch_cuda):
                 view(ptr.value, offs[1], (b, nl))
             assert L.xattn_fp32_partial(q.data_ptr(), kl.data_ptr(), vl.data_ptr(), po.data_ptr(),
                                         pm.data_ptr(), pl.data_ptr(), b, nl, hi - lo, d, None) == 0
-        bases = (ctypes.c_void_p * 3)(*ptrs)
-        assert L.xattn_peer_merge(bases, 3, -1, b * nl, d, 1, None) == 0
+        bases = (ctypes.c_void_p * len(ptrs))(*ptrs)
+        assert L.xattn_peer_merge(bases, len(ptrs), -1, b * nl, d, 1, None) == 0
         torch.cuda.synchronize()
         ref = ref_attention(torch, q, k, v)
         outs = [view(p, offs[3], (b, nl, d)).clone() for p in ptrs]
